@@ -1,0 +1,67 @@
+// Error objects, per-thread last-error message and device queries of the C ABI.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "amcu_internal.h"
+
+namespace amcu {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+am_status_code set_error(am_status_code code, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int num_sms() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    return n;
+}
+
+}  // namespace amcu
+
+namespace {
+// Error object of the reference C ABI (src/c_api_error.cpp:14-41): a status
+// code plus an owned message.
+struct ErrorObject {
+    am_status_code code;
+    std::string message;
+};
+}  // namespace
+
+extern "C" {
+
+const char* amcu_last_error(void) { return amcu::g_last_error.c_str(); }
+
+const char* amcu_version(void) { return "aethermind_b200 0.1 (sm_100a)"; }
+
+am_error_handle am_error_create(am_status_code code, const char* message) {
+    return new ErrorObject{code, message ? message : ""};
+}
+
+void am_error_destroy(am_error_handle e) { delete static_cast<ErrorObject*>(e); }
+
+am_status_code am_error_code(am_error_handle e) {
+    return e ? static_cast<ErrorObject*>(e)->code : AM_STATUS_OK;
+}
+
+const char* am_error_message(am_error_handle e) {
+    return e ? static_cast<ErrorObject*>(e)->message.c_str() : "";
+}
+
+}  // extern "C"

@@ -1,0 +1,487 @@
+// Weight-only dequant GEMV for decode (m <= 8) and the weight prepacker.
+//
+// Device weight format ("tile16x64"): the [N, K] weight is cut into tiles of
+// 16 output rows x 64 input columns, stored tile after tile with K fastest
+// (tile (rb, c) at index rb * K/64 + c). Inside a tile, lane L = 4g + t of a
+// warp owns rows {g, g+8} x columns [16t, 16t+16): exactly the A-operand
+// fragments of four m16n8k16 tensor-core MMAs in which MMA j contracts
+// columns 16t+4j .. 16t+4j+3 of this lane (the MMA's k-slot -> column map is a
+// free choice as long as the activation fragment uses the same one). One
+// 16-byte (INT4) or 32-byte (INT8) coalesced load per lane per tile feeds the
+// MMAs with no shuffles; the activations for the same columns are 32
+// contiguous bytes per lane.
+//   INT4 word j of lane L: nibble p at bits 4p, value +8 offset-binary is NOT
+//        used: nibbles hold two's-complement q. p0,p4,p2,p6 = row g columns
+//        +0,+1,+2,+3 and p1,p5,p3,p7 = row g+8 columns +0,+1,+2,+3, so
+//        (word >> 4i) & 0x000F000F yields MMA register i directly.
+//   INT8: 32 bytes per lane: row g columns [16t, 16t+16) then row g+8.
+//   INT4 scales: [N/16][K/128][16] fp16 with slot 2g = row g, 2g+1 = row g+8.
+//   INT8 scales: fp32 [N] (device row order).
+// Gate/up fusion: rows 0-7 of every tile are gate rows 8*rb..8*rb+7 and rows
+// 8-15 the matching up rows, so one lane holds gate and up of the same output
+// and the SiLU-Mul epilogue needs no data exchange.
+#include "../amcu_internal.h"
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace amcu {
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// INT4 word -> 4 bf16x2 MMA registers holding the exact integers q.
+__device__ __forceinline__ void unpack_w4_word(uint32_t w, uint32_t (&a)[4]) {
+    // (w >> 4i) & 0x000F000F selects two nibbles; XOR with 0x43084308 maps the
+    // two's-complement nibble n to bf16 bits of 128 + (n ^ 8) = 136 + q
+    // (exact: integers up to 256 are representable); subtracting 136 gives q.
+    const uint32_t bias = 0x43084308u;  // bf16x2 (136, 136)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint32_t v;
+        const uint32_t s = w >> (4 * i);
+        asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(v) : "r"(s), "r"(0x000F000Fu), "r"(bias));  // (a & b) ^ c
+        __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
+        const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&bias);
+        h = __hsub2(h, b);
+        a[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+}
+
+// Four int8 values -> two bf16x2 (bytes 0,1) and (bytes 2,3); exact.
+__device__ __forceinline__ void unpack_w8_word(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const uint32_t u = w ^ 0x80808080u;  // offset binary: q + 128
+    float f[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t bits = __byte_perm(u, 0x4B000000u, 0x7650u + i);  // 0x4B0000bb = 2^23 + bb
+        f[i] = __uint_as_float(bits) - 8388736.0f;                      // - (2^23 + 128)
+    }
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(f[0], f[1]);
+    __nv_bfloat162 p1 = __floats2bfloat162_rn(f[2], f[3]);
+    lo = *reinterpret_cast<uint32_t*>(&p0);
+    hi = *reinterpret_cast<uint32_t*>(&p1);
+}
+
+template <typename T>
+__device__ __forceinline__ T epi_store(float v) { return Act<T>::store(v); }
+
+// One CTA = one 16-row tile of W; its warps split K. m <= 8 activation rows.
+template <int FMT, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) gemv_tc_kernel(GemvParams p) {
+    constexpr int W = kGemvThreads / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int64_t rb = blockIdx.x;
+    const int64_t C = p.k / 64;
+    const int64_t per = (C + W - 1) / W;
+    const int64_t c0 = warp * per;
+    const int64_t c1 = c0 + per < C ? c0 + per : C;
+    const bool has_x = g < p.m;
+    const __nv_bfloat16* xrow = static_cast<const __nv_bfloat16*>(p.x) + (has_x ? g : 0) * p.x_stride;
+
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    constexpr int kTileBytes = FMT == AMCU_WFMT_INT4 ? 512 : 1024;
+    const uint8_t* wbase = static_cast<const uint8_t*>(p.w) + (rb * C) * kTileBytes;
+    const int64_t G = p.k / 128;
+
+    constexpr int U = 4;
+    for (int64_t cb = c0; cb < c1; cb += U) {
+        uint4 wv[U][FMT == AMCU_WFMT_INT4 ? 1 : 2];
+        uint4 xv[U][2];
+        uint32_t sv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t c = cb + u;
+            if (c < c1) {
+                const uint8_t* tp = wbase + c * kTileBytes;
+                if constexpr (FMT == AMCU_WFMT_INT4) {
+                    wv[u][0] = ld_stream_u4(tp + lane * 16);
+                    sv[u] = *reinterpret_cast<const uint32_t*>(static_cast<const __half*>(p.scales) +
+                                                               ((rb * G + (c >> 1)) * 16 + 2 * g));
+                } else {
+                    wv[u][0] = ld_stream_u4(tp + lane * 32);
+                    wv[u][1] = ld_stream_u4(tp + lane * 32 + 16);
+                }
+                if (has_x) {
+                    const __nv_bfloat16* xp = xrow + c * 64 + 16 * t;
+                    xv[u][0] = ld_u4(xp);
+                    xv[u][1] = ld_u4(xp + 8);
+                } else {
+                    xv[u][0] = make_uint4(0, 0, 0, 0);
+                    xv[u][1] = make_uint4(0, 0, 0, 0);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (cb + u < c1) {
+                const uint32_t X[8] = {xv[u][0].x, xv[u][0].y, xv[u][0].z, xv[u][0].w,
+                                       xv[u][1].x, xv[u][1].y, xv[u][1].z, xv[u][1].w};
+                if constexpr (FMT == AMCU_WFMT_INT4) {
+                    float part[4] = {0.f, 0.f, 0.f, 0.f};
+                    const uint32_t words[4] = {wv[u][0].x, wv[u][0].y, wv[u][0].z, wv[u][0].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t a[4];
+                        unpack_w4_word(words[j], a);
+                        mma_bf16_16816(part, a, X[2 * j], X[2 * j + 1]);
+                    }
+                    const __half2 s2 = *reinterpret_cast<const __half2*>(&sv[u]);
+                    const float s_lo = __low2float(s2), s_hi = __high2float(s2);
+                    acc[0] = fmaf(part[0], s_lo, acc[0]);
+                    acc[1] = fmaf(part[1], s_lo, acc[1]);
+                    acc[2] = fmaf(part[2], s_hi, acc[2]);
+                    acc[3] = fmaf(part[3], s_hi, acc[3]);
+                } else {
+                    const uint32_t rg[4] = {wv[u][0].x, wv[u][0].y, wv[u][0].z, wv[u][0].w};
+                    const uint32_t rh[4] = {wv[u][1].x, wv[u][1].y, wv[u][1].z, wv[u][1].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t a[4];
+                        unpack_w8_word(rg[j], a[0], a[2]);
+                        unpack_w8_word(rh[j], a[1], a[3]);
+                        mma_bf16_16816(acc, a, X[2 * j], X[2 * j + 1]);
+                    }
+                }
+            }
+        }
+    }
+
+    // Cross-warp reduction of the 16 x 8 accumulator tile.
+    __shared__ float red[W][32][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[warp][lane][i] = acc[i];
+    __syncthreads();
+    if (warp != 0) return;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < W; ++w) s += red[w][lane][i];
+        acc[i] = s;
+    }
+    __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
+    const int m0 = 2 * t, m1 = 2 * t + 1;
+    if constexpr (EPI == AMCU_EPI_SILU_MUL) {
+        // c0/c1: gate row, c2/c3: up row of output column 8*rb + g.
+        const int64_t col = rb * 8 + g;
+        if (m0 < p.m) {
+            float gt = Act<__nv_bfloat16>::round(acc[0]), up = Act<__nv_bfloat16>::round(acc[2]);
+            y[m0 * p.y_stride + col] = epi_store<__nv_bfloat16>(silu_ref(gt) * up);
+        }
+        if (m1 < p.m) {
+            float gt = Act<__nv_bfloat16>::round(acc[1]), up = Act<__nv_bfloat16>::round(acc[3]);
+            y[m1 * p.y_stride + col] = epi_store<__nv_bfloat16>(silu_ref(gt) * up);
+        }
+    } else {
+        const int64_t n_lo = rb * 16 + g, n_hi = n_lo + 8;
+        float s_lo = 1.f, s_hi = 1.f;
+        if constexpr (FMT == AMCU_WFMT_INT8) {
+            s_lo = static_cast<const float*>(p.scales)[n_lo];
+            s_hi = static_cast<const float*>(p.scales)[n_hi];
+        }
+        const float v[4] = {acc[0] * s_lo, acc[1] * s_lo, acc[2] * s_hi, acc[3] * s_hi};
+        const int ms[4] = {m0, m1, m0, m1};
+        const int64_t ns[4] = {n_lo, n_lo, n_hi, n_hi};
+        const __nv_bfloat16* res = static_cast<const __nv_bfloat16*>(p.residual);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (ms[i] < p.m) {
+                const int64_t off = ms[i] * p.y_stride + ns[i];
+                float o = Act<__nv_bfloat16>::round(v[i]);
+                if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD) o = o + __bfloat162float(res[off]);
+                y[off] = epi_store<__nv_bfloat16>(o);
+            }
+        }
+    }
+}
+
+// Plain fp32 weights (the fp32 tiny model): one thread per output, fp32 FMA.
+template <typename T, int EPI>
+__global__ void gemm_plain_kernel(GemvParams p) {
+    const int64_t n = blockIdx.x * 32 + (threadIdx.x & 31);
+    const int64_t m = blockIdx.y * 8 + (threadIdx.x >> 5);
+    const int64_t n_out = EPI == AMCU_EPI_SILU_MUL ? p.n / 2 : p.n;
+    if (m >= p.m || n >= n_out) return;
+    const T* x = static_cast<const T*>(p.x) + m * p.x_stride;
+    const T* w = static_cast<const T*>(p.w);
+    auto dot = [&](int64_t row) {
+        const T* wr = w + row * p.k;
+        float acc = 0.f;
+        for (int64_t k = 0; k < p.k; ++k) acc = fmaf(Act<T>::load(x[k]), Act<T>::load(wr[k]), acc);
+        return acc;
+    };
+    T* y = static_cast<T*>(p.y);
+    if constexpr (EPI == AMCU_EPI_SILU_MUL) {
+        // plain gate/up weight is [gate; up] stacked (2I rows)
+        const float gt = Act<T>::round(dot(n)), up = Act<T>::round(dot(n + n_out));
+        y[m * p.y_stride + n] = Act<T>::store(silu_ref(gt) * up);
+    } else {
+        float o = Act<T>::round(dot(n));
+        if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD)
+            o = o + Act<T>::load(static_cast<const T*>(p.residual)[m * p.y_stride + n]);
+        y[m * p.y_stride + n] = Act<T>::store(o);
+    }
+}
+
+template <int FMT>
+static void launch_gemv_fmt(const GemvParams& p, int epi, cudaStream_t s) {
+    const dim3 grid((unsigned)(p.n / 16));
+    switch (epi) {
+        case AMCU_EPI_STORE: gemv_tc_kernel<FMT, AMCU_EPI_STORE><<<grid, kGemvThreads, 0, s>>>(p); break;
+        case AMCU_EPI_RESIDUAL_ADD: gemv_tc_kernel<FMT, AMCU_EPI_RESIDUAL_ADD><<<grid, kGemvThreads, 0, s>>>(p); break;
+        default: gemv_tc_kernel<FMT, AMCU_EPI_SILU_MUL><<<grid, kGemvThreads, 0, s>>>(p); break;
+    }
+}
+
+void launch_gemv(const GemvParams& p, int fmt, int epi, cudaStream_t s) {
+    if (fmt == AMCU_WFMT_INT4) launch_gemv_fmt<AMCU_WFMT_INT4>(p, epi, s);
+    else launch_gemv_fmt<AMCU_WFMT_INT8>(p, epi, s);
+}
+
+void launch_gemm_plain(const GemvParams& p, int dtype, int epi, cudaStream_t s) {
+    const int64_t n_out = epi == AMCU_EPI_SILU_MUL ? p.n / 2 : p.n;
+    const dim3 grid((unsigned)ceil_div(n_out, 32), (unsigned)ceil_div(p.m, 8));
+#define AMCU_PL(T, E) gemm_plain_kernel<T, E><<<grid, 256, 0, s>>>(p)
+    if (dtype == AMCU_F32) {
+        if (epi == AMCU_EPI_STORE) AMCU_PL(float, AMCU_EPI_STORE);
+        else if (epi == AMCU_EPI_RESIDUAL_ADD) AMCU_PL(float, AMCU_EPI_RESIDUAL_ADD);
+        else AMCU_PL(float, AMCU_EPI_SILU_MUL);
+    } else {
+        if (epi == AMCU_EPI_STORE) AMCU_PL(__nv_bfloat16, AMCU_EPI_STORE);
+        else if (epi == AMCU_EPI_RESIDUAL_ADD) AMCU_PL(__nv_bfloat16, AMCU_EPI_RESIDUAL_ADD);
+        else AMCU_PL(__nv_bfloat16, AMCU_EPI_SILU_MUL);
+    }
+#undef AMCU_PL
+}
+
+// ---------------------------------------------------------------------------
+// Prepack / unpack between the canonical and the tile16x64 formats.
+// ---------------------------------------------------------------------------
+// Device row r -> (source, canonical row). With gate/up interleave, tile rows
+// 0-7 come from gate rows 8*rb.., rows 8-15 from the matching up rows.
+__device__ __forceinline__ int64_t src_row(int64_t r, bool il, int& which) {
+    if (!il) { which = 0; return r; }
+    const int64_t rb = r >> 4, rr = r & 15;
+    which = rr >= 8;
+    return rb * 8 + (rr & 7);
+}
+
+// INT4: one thread per 32-bit device word.
+__global__ void pack_w4_kernel(const uint8_t* __restrict__ a, const uint8_t* __restrict__ b, bool il,
+                               int64_t N, int64_t K, uint32_t* __restrict__ out, bool unpack,
+                               uint8_t* __restrict__ canon_out) {
+    const int64_t words = N * K / 8;
+    const int64_t C = K / 64;
+    for (int64_t wi = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; wi < words; wi += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t tile = wi / 128;  // 512 B per tile = 128 words
+        const int in_tile = (int)(wi % 128);
+        const int lane = in_tile >> 2, j = in_tile & 3;
+        const int g = lane >> 2, t = lane & 3;
+        const int64_t rb = tile / C, c = tile % C;
+        const int64_t col0 = c * 64 + 16 * t + 4 * j;
+        // nibble p -> (row offset, column offset)
+        const int prow[8] = {0, 8, 0, 8, 0, 8, 0, 8};
+        const int pcol[8] = {0, 0, 2, 2, 1, 1, 3, 3};
+        if (!unpack) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int pp = 0; pp < 8; ++pp) {
+                int which;
+                const int64_t r = src_row(rb * 16 + g + prow[pp], il, which);
+                const uint8_t* src = which ? b : a;
+                const int64_t col = col0 + pcol[pp];
+                const uint8_t byte = src[r * (K / 2) + col / 2];
+                const uint32_t nib = (col & 1) ? (byte >> 4) : (byte & 15u);
+                word |= nib << (4 * pp);
+            }
+            out[wi] = word;
+        } else {
+            const uint32_t word = out[wi];
+#pragma unroll
+            for (int pp = 0; pp < 4; ++pp) {
+                // nibbles pp and pp+4 hold columns col (even) and col+1 of one row
+                const int64_t r = rb * 16 + g + prow[pp];
+                const int64_t col = col0 + pcol[pp];
+                const uint32_t lo = (word >> (4 * pp)) & 15u, hi = (word >> (4 * (pp + 4))) & 15u;
+                canon_out[r * (K / 2) + col / 2] = (uint8_t)(lo | (hi << 4));
+            }
+        }
+    }
+}
+
+// INT4 scales: canonical fp16 [N][G] -> [N/16][G][16] with slot 2g = row g, 2g+1 = row g+8.
+__global__ void pack_s4_kernel(const __half* __restrict__ a, const __half* __restrict__ b, bool il, int64_t N,
+                               int64_t G, __half* __restrict__ out, bool unpack) {
+    const int64_t total = N * G;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t rb = i / (G * 16);
+        const int64_t grp = (i / 16) % G;
+        const int slot = (int)(i % 16);
+        const int64_t r_dev = rb * 16 + (slot >> 1) + ((slot & 1) ? 8 : 0);
+        int which;
+        const int64_t r = src_row(r_dev, il, which);
+        if (!unpack) out[i] = (which ? b : a)[r * G + grp];
+        else const_cast<__half*>(a)[r_dev * G + grp] = out[i];
+    }
+}
+
+// INT8: one thread per 16-byte half-lane chunk.
+__global__ void pack_w8_kernel(const int8_t* __restrict__ a, const int8_t* __restrict__ b, bool il, int64_t N,
+                               int64_t K, uint4* __restrict__ out, bool unpack) {
+    const int64_t chunks = N * K / 16;
+    const int64_t C = K / 64;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < chunks; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t tile = i / 64;  // 1024 B per tile
+        const int in_tile = (int)(i % 64);
+        const int lane = in_tile >> 1, half = in_tile & 1;
+        const int g = lane >> 2, t = lane & 3;
+        const int64_t rb = tile / C, c = tile % C;
+        const int64_t r_dev = rb * 16 + g + (half ? 8 : 0);
+        const int64_t col = c * 64 + 16 * t;
+        if (!unpack) {
+            int which;
+            const int64_t r = src_row(r_dev, il, which);
+            out[i] = *reinterpret_cast<const uint4*>((which ? b : a) + r * K + col);
+        } else {
+            *reinterpret_cast<uint4*>(const_cast<int8_t*>(a) + r_dev * K + col) = out[i];
+        }
+    }
+}
+
+__global__ void pack_s8_kernel(const float* __restrict__ a, const float* __restrict__ b, bool il, int64_t N,
+                               float* __restrict__ out) {
+    for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < N; r += (int64_t)gridDim.x * blockDim.x) {
+        int which;
+        const int64_t s = src_row(r, il, which);
+        out[r] = (which ? b : a)[s];
+    }
+}
+
+__global__ void copy_bytes_kernel(const uint8_t* __restrict__ a, const uint8_t* __restrict__ b, int64_t half_bytes,
+                                  uint8_t* __restrict__ out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < 2 * half_bytes; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = i < half_bytes ? a[i] : b[i - half_bytes];
+}
+
+}  // namespace amcu
+
+using namespace amcu;
+
+namespace {
+int pack_grid(int64_t n) {
+    int64_t b = (n + 255) / 256;
+    if (b > 148 * 32) b = 148 * 32;
+    return (int)(b < 1 ? 1 : b);
+}
+int plain_elt(int32_t dtype) { return dtype == AMCU_F32 ? 4 : 2; }
+
+am_status_code check_weight_shape(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group) {
+    AMCU_REQUIRE(n > 0 && k > 0, "weight: n and k must be positive");
+    if (format == AMCU_WFMT_PLAIN) {
+        AMCU_REQUIRE(dtype == AMCU_F32 || dtype == AMCU_BF16, "plain weight dtype must be f32 or bf16");
+        return AM_STATUS_OK;
+    }
+    AMCU_REQUIRE(format == AMCU_WFMT_INT8 || format == AMCU_WFMT_INT4, "unknown weight format %d", format);
+    AMCU_REQUIRE(n % 16 == 0, "quantized weight: n (%lld) must be a multiple of 16", (long long)n);
+    AMCU_REQUIRE(k % 64 == 0, "quantized weight: k (%lld) must be a multiple of 64", (long long)k);
+    if (format == AMCU_WFMT_INT4) {
+        AMCU_REQUIRE(group == 128, "int4 weight: only group size 128 is supported");
+        AMCU_REQUIRE(k % 128 == 0, "int4 weight: k must be a multiple of 128");
+    }
+    return AM_STATUS_OK;
+}
+
+am_status_code prepack_impl(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group, const void* qa,
+                            const void* sa, const void* qb, const void* sb, bool il, void* qp, void* sp,
+                            cudaStream_t s) {
+    if (format == AMCU_WFMT_PLAIN) {
+        if (!il) {
+            cudaMemcpyAsync(qp, qa, (size_t)n * k * plain_elt(dtype), cudaMemcpyDeviceToDevice, s);
+        } else {
+            const int64_t hb = n / 2 * k * plain_elt(dtype);
+            copy_bytes_kernel<<<pack_grid(2 * hb), 256, 0, s>>>((const uint8_t*)qa, (const uint8_t*)qb, hb,
+                                                               (uint8_t*)qp);
+        }
+    } else if (format == AMCU_WFMT_INT4) {
+        pack_w4_kernel<<<pack_grid(n * k / 8), 256, 0, s>>>((const uint8_t*)qa, (const uint8_t*)qb, il, n, k,
+                                                           (uint32_t*)qp, false, nullptr);
+        pack_s4_kernel<<<pack_grid(n * (k / 128)), 256, 0, s>>>((const __half*)sa, (const __half*)sb, il, n,
+                                                                k / 128, (__half*)sp, false);
+    } else {
+        pack_w8_kernel<<<pack_grid(n * k / 16), 256, 0, s>>>((const int8_t*)qa, (const int8_t*)qb, il, n, k,
+                                                            (uint4*)qp, false);
+        pack_s8_kernel<<<pack_grid(n), 256, 0, s>>>((const float*)sa, (const float*)sb, il, n, (float*)sp);
+    }
+    return check_launch("amcu_prepack_weight");
+}
+}  // namespace
+
+extern "C" {
+
+int64_t amcu_packed_weight_bytes(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group) {
+    (void)group;
+    if (format == AMCU_WFMT_PLAIN) return n * k * plain_elt(dtype);
+    if (format == AMCU_WFMT_INT8) return n * k;
+    return n * k / 2;
+}
+
+int64_t amcu_packed_scale_bytes(int32_t format, int64_t n, int64_t k, int64_t group) {
+    if (format == AMCU_WFMT_INT8) return n * 4;
+    if (format == AMCU_WFMT_INT4) return n * (k / (group > 0 ? group : 128)) * 2;
+    return 0;
+}
+
+am_status_code amcu_prepack_weight(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group,
+                                   const void* q, const void* sc, void* qp, void* sp, void* stream) {
+    clear_error();
+    am_status_code st = check_weight_shape(format, dtype, n, k, group);
+    if (st != AM_STATUS_OK) return st;
+    AMCU_REQUIRE(q && qp, "amcu_prepack_weight: null pointer");
+    AMCU_REQUIRE(format == AMCU_WFMT_PLAIN || (sc && sp), "amcu_prepack_weight: null scale pointer");
+    AMCU_REQUIRE(aligned(qp, 16) && aligned(q, 16), "amcu_prepack_weight: weights must be 16-byte aligned");
+    return prepack_impl(format, dtype, n, k, group, q, sc, q, sc, false, qp, sp, as_stream(stream));
+}
+
+am_status_code amcu_prepack_gate_up(int32_t format, int32_t dtype, int64_t inter, int64_t k, int64_t group,
+                                    const void* gq, const void* gs, const void* uq, const void* us, void* qp,
+                                    void* sp, void* stream) {
+    clear_error();
+    AMCU_REQUIRE(inter > 0 && inter % 8 == 0, "amcu_prepack_gate_up: inter must be a positive multiple of 8");
+    am_status_code st = check_weight_shape(format, dtype, 2 * inter, k, group);
+    if (st != AM_STATUS_OK) return st;
+    AMCU_REQUIRE(gq && uq && qp, "amcu_prepack_gate_up: null pointer");
+    AMCU_REQUIRE(format == AMCU_WFMT_PLAIN || (gs && us && sp), "amcu_prepack_gate_up: null scale pointer");
+    AMCU_REQUIRE(aligned(qp, 16) && aligned(gq, 16) && aligned(uq, 16), "amcu_prepack_gate_up: misaligned");
+    return prepack_impl(format, dtype, 2 * inter, k, group, gq, gs, uq, us, true, qp, sp, as_stream(stream));
+}
+
+am_status_code amcu_unpack_weight(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group,
+                                  const void* qp, const void* sp, void* q, void* sc, void* stream) {
+    clear_error();
+    am_status_code st = check_weight_shape(format, dtype, n, k, group);
+    if (st != AM_STATUS_OK) return st;
+    AMCU_REQUIRE(q && qp, "amcu_unpack_weight: null pointer");
+    cudaStream_t s = as_stream(stream);
+    if (format == AMCU_WFMT_PLAIN) {
+        cudaMemcpyAsync(q, qp, (size_t)n * k * plain_elt(dtype), cudaMemcpyDeviceToDevice, s);
+    } else if (format == AMCU_WFMT_INT4) {
+        pack_w4_kernel<<<pack_grid(n * k / 8), 256, 0, s>>>(nullptr, nullptr, false, n, k,
+                                                           (uint32_t*)const_cast<void*>(qp), true, (uint8_t*)q);
+        if (sc && sp)
+            pack_s4_kernel<<<pack_grid(n * (k / 128)), 256, 0, s>>>((const __half*)sc, nullptr, false, n, k / 128,
+                                                                    (__half*)const_cast<void*>(sp), true);
+    } else {
+        pack_w8_kernel<<<pack_grid(n * k / 16), 256, 0, s>>>((const int8_t*)q, nullptr, false, n, k,
+                                                            (uint4*)const_cast<void*>(qp), true);
+        if (sc && sp) cudaMemcpyAsync(sc, sp, (size_t)n * 4, cudaMemcpyDeviceToDevice, s);
+    }
+    return check_launch("amcu_unpack_weight");
+}
+
+}  // extern "C"

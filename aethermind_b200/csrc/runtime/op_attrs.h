@@ -1,0 +1,33 @@
+// Per-op attribute PODs carried in KernelContext::attrs (the reference passes
+// e.g. RMSNorm eps the same way, src/operators/rmsnorm_op.cpp:26-27).
+#pragma once
+#include <cstdint>
+
+namespace aethermind {
+
+struct RmsNormAttrs {
+    float eps;
+};
+struct LinearAttrs {
+    int32_t epilogue;  // amcu_epilogue
+};
+struct RopeKvAttrs {
+    double theta;
+    int64_t rows_per_seq, capacity, slot_stride, n_q, n_kv, head_dim;
+    const int32_t* seq_pos;
+    int32_t* status;
+};
+struct AttentionAttrs {
+    int64_t rows_per_seq, capacity, slot_stride, n_q, n_kv, head_dim, max_context;
+    const int32_t* seq_pos;
+    int32_t num_splits;
+};
+struct EmbeddingAttrs {
+    const float* row_scales;
+    int32_t* status;
+};
+struct ArgmaxAttrs {
+    float* gap_out;
+};
+
+}  // namespace aethermind

@@ -1,0 +1,319 @@
+"""Benchmark of the Llama decode/prefill hot path on B200.
+
+Workload (N=1): the Llama-3-8B-shaped model with INT4 group-128 weight-only
+quantization and bf16 activations/KV, synthetic seeded
+random-init weights, batch 1, a 512-token prompt of uniform token ids and
+256 greedy decode tokens, static KV capacity 4096. One "step" is one full
+greedy generation (prefill 512 + 256 decode tokens) through the engine.
+
+  value  decode tok/s = decoded tokens / device decode time (CUDA events in
+         the engine around the replayed decode graphs; prompt ids are already
+         staged on the device before that region).
+  e2e    generated tok/s of the public am_session_generate call, host token
+         ids in and out, pinned H2D/D2H inside the timed region.
+  roofline  the dominant kernel, the W4 GEMV, timed alone with CUDA events on
+         the 8B shapes, weights rotated over >L2 buffers (cold HBM).
+  cpu_baseline  the CPU oracle's greedy decode of the same synthetic model on
+         the host cores (bounded sample, see "sample").
+
+With --gpus N > 1 (torchrun), the model is tensor-parallel over N GPUs
+(one NCCL all-reduce per attention and per MLP block); total work is fixed
+("strong" scaling) and timing is the max over ranks.
+--impl reference times the reference-side CPU implementation (the oracle
+restatement; the reference engine itself cannot run a Llama forward) on the
+same config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PROMPT = 512
+NEW = 256
+SEED = 0
+METRIC = "decode tok/s bs=1 (8B W4 g128, 512-token prompt, 256 greedy tokens)"
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    def __init__(self, index: int = 0):
+        self.index = index
+        self.rows: list[list[str]] = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        def run():
+            q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                         timeout=5).stdout.strip()
+                    if out:
+                        self.rows.append([c.strip() for c in out.split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+
+    def stop(self) -> dict:
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            for i, n in enumerate(names):
+                if len(r) > 5 + i and r[5 + i].lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def gemv_roofline(hbm_peak: float) -> dict:
+    """Times the W4 GEMV of the 8B gate/up projection (N = 2 x 14336, K = 4096)
+    alone, rotating over enough weight copies that every launch reads HBM."""
+    import ctypes as C
+
+    import torch
+
+    from aethermind_b200 import _lib as L
+    from aethermind_b200 import ops
+
+    n, k = 2 * 14336, 4096
+    q, s = ops.synth_w4(SEED, 99, n, k, 0.004)
+    copies = []
+    per = n * k // 2 + n * (k // 128) * 2
+    ncopy = max(2, int(512e6 // per) + 1)  # > 4 x L2
+    for _ in range(ncopy):
+        copies.append(ops.prepack(L.WFMT_INT4, q, s, n, k))
+    x = torch.randn(1, k, device="cuda").to(torch.bfloat16)
+    y = torch.empty(1, n, device="cuda", dtype=torch.bfloat16)
+    args = []
+    for pw in copies:
+        a, _, _ = ops._linear_args(x, pw, L.EPI_STORE, None, y)
+        args.append(a)
+    lib = L.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    for a in args[:4]:
+        lib.amcu_gemv_w4g128(C.byref(a), stream)
+    torch.cuda.synchronize()
+    reps = 20 * ncopy
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(reps):
+        lib.amcu_gemv_w4g128(C.byref(args[i % ncopy]), stream)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    alg = n * k // 2 + n * (k // 128) * 2 + k * 2 + n * 2
+    gbs = alg / (us * 1e-6) / 1e9
+    del copies
+    torch.cuda.empty_cache()
+    return {"kernel": "gemv_tc_kernel<INT4> (8B gate_up, n=28672 k=4096, m=1)", "bound": "hbm",
+            "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(gbs / hbm_peak, 3),
+            "traffic": None, "alg_bytes_per_launch": alg, "us_per_launch": round(us, 2)}
+
+
+def decode_bytes_per_token(cfg, ctx: float) -> float:
+    H, I, d = cfg.hidden, cfg.inter, cfg.head_dim
+    qkv = (cfg.n_q_heads + 2 * cfg.n_kv_heads) * d
+    per_layer = H * qkv + cfg.n_q_heads * d * H + 2 * I * H + I * H
+    params = cfg.layers * per_layer + cfg.vocab * H
+    w = params / 2 + params / 128 * 2
+    kv = cfg.layers * 2 * cfg.n_kv_heads * d * 2 * ctx
+    return w + kv
+
+
+def cpu_oracle_decode(cfg, prompt_len: int, new: int, layers: int | None = None) -> dict:
+    """Greedy decode of the synthetic model by the CPU oracle; returns tok/s of
+    the decode phase (all host threads via OpenMP)."""
+    import numpy as np
+
+    import oracle
+
+    t0 = time.time()
+    om = oracle.synthetic_oracle_model(cfg, SEED, layers=layers)
+    if layers is not None:
+        om.m.layers = layers
+    gen_s = time.time() - t0
+    prompt = np.random.default_rng(SEED).integers(0, cfg.vocab, prompt_len).astype(np.int64)
+    t1 = time.time()
+    om.generate(prompt, 1)
+    t_prefill = time.time() - t1
+    t2 = time.time()
+    om.generate(prompt, 1 + new)
+    t_total = time.time() - t2
+    dec = max(t_total - t_prefill, 1e-9)
+    return {"tok_s": new / dec, "prefill_s": t_prefill, "weights_gen_s": gen_s,
+            "cores": os.cpu_count()}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from aethermind_b200.session import LLAMA_8B_W4
+    import dataclasses
+    cfg = dataclasses.replace(LLAMA_8B_W4, max_seq=PROMPT + NEW)
+    steps = []
+    for _ in range(args.warmup + args.steps):
+        steps.append(cpu_oracle_decode(cfg, 8, 2))
+    timed = steps[args.warmup:]
+    v = statistics.mean(s["tok_s"] for s in timed)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * 2 / v, 1),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded integer-hash INT4 weights, uniform token ids)",
+            "config": {"workload": "llama3-8b-shape W4 g128 bs=1 decode", "global_batch": 1, "seq_len": PROMPT + NEW,
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": "per step: 8-token prompt prefill + 2 greedy decode tokens of the full 32-layer "
+                                       "8B W4 model; decode tok/s (CPU restatement in oracle/am_oracle.c, OpenMP)"},
+            "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="aethermind_b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-roofline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None, help="debug: fewer layers (invalidates the number)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import dataclasses
+
+    import numpy as np
+    import torch
+
+    from aethermind_b200 import session
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    nccl_id = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        obj = [session.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+
+    cfg = dataclasses.replace(session.LLAMA_8B_W4, max_seq=4096)
+    if args.layers:
+        cfg = dataclasses.replace(cfg, layers=args.layers)
+    rt = session.Runtime(local, rank, world, nccl_id)
+    model = session.Model(rt, cfg)
+    model.init_synthetic(SEED)
+    sess = session.Session(model)
+    prompt = np.random.default_rng(SEED).integers(0, cfg.vocab, PROMPT).astype(np.uint32)
+
+    for _ in range(args.warmup):
+        sess.generate(prompt, NEW)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    dec_ms, pre_ms, wall = [], [], []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        toks = sess.generate(prompt, NEW)
+        wall.append(time.perf_counter() - t0)
+        p, d, n = sess.timing()
+        pre_ms.append(p)
+        dec_ms.append(d)
+    torch.cuda.synchronize()
+    ck = clocks.stop()
+    if dist:
+        dist.barrier()
+        t = torch.tensor([sum(dec_ms), sum(pre_ms), sum(wall)], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dec_total, pre_total, wall_total = t.tolist()
+    else:
+        dec_total, pre_total, wall_total = sum(dec_ms), sum(pre_ms), sum(wall)
+
+    decoded = args.steps * (NEW - 1)
+    value = decoded / (dec_total / 1e3)
+    hbm_peak, tc_peak, peak_kind = _peaks()
+    ctx_mean = PROMPT + NEW / 2
+    bpt = decode_bytes_per_token(cfg, ctx_mean) / world
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round((dec_total + pre_total) / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded integer-hash INT4 weights, uniform token ids)",
+        "config": {"workload": "llama3-8b-shape W4 g128 bs=1: prefill 512 + 256 greedy decode", "global_batch": 1,
+                   "seq_len": PROMPT + NEW, "parallelism": f"tp{world}",
+                   "l2": "weights (3.9 GB) exceed L2; no flush needed", "layers": cfg.layers},
+        "prefill_tok_s": round(args.steps * PROMPT / (pre_total / 1e3), 1),
+        "decode_ms_per_token": round(dec_total / decoded, 4),
+        "decode_hbm_gbs_per_gpu": round(bpt * value / 1e9, 1),
+        "decode_hbm_frac_per_gpu": round(bpt * value / 1e9 / hbm_peak, 3),
+        "peaks": {"hbm_gbs": hbm_peak, "bf16_tflops": tc_peak, "kind": peak_kind},
+        "clocks": ck,
+        "e2e": {"value": round(args.steps * NEW / wall_total, 2),
+                "unit": "tok/s (am_session_generate: 512-token prompt in, 256 tokens out, host buffers)",
+                "h2d_bytes_per_step": PROMPT * 8, "d2h_bytes_per_step": NEW * 12 + 4},
+        "gpu_launches": None,
+    }
+    # kernel launches of this library in the timed region (from the plans)
+    try:
+        dec_steps = sess.plan_steps(1, 1, 1)
+        pre_steps = sess.plan_steps(0, 1, PROMPT)
+        n_dec = sum(1 for l in dec_steps if "<host>" not in l) + sum(1 for l in dec_steps if "AttnDecode" in l) + 1
+        lin = sum(1 for l in pre_steps if "Gemm" in l)
+        n_pre = sum(1 for l in pre_steps if "<host>" not in l) + lin * (PROMPT // 8 - 1) + 1
+        line["gpu_launches"] = args.steps * (n_pre + (NEW - 1) * n_dec)
+    except Exception as e:  # pragma: no cover
+        line["gpu_launches_error"] = str(e)
+    if rank == 0 and world == 1 and not args.no_roofline:
+        del sess, model
+        torch.cuda.empty_cache()
+        line["roofline"] = gemv_roofline(hbm_peak)
+        line["roofline"]["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_oracle_decode(dataclasses.replace(cfg, max_seq=64), 8, 2)
+        line["cpu_baseline"] = {"value": round(cb["tok_s"], 4), "unit": "tok/s", "cores": cb["cores"], "kind": "port",
+                                "sample": "8-token prompt + 2 greedy decode tokens of the same 32-layer 8B W4 "
+                                          "synthetic model (oracle/am_oracle.c, OpenMP on all host threads)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

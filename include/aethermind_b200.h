@@ -1,0 +1,404 @@
+/*
+ * aethermind_b200 -- C ABI of the B200-native Llama prefill/decode hot path.
+ *
+ * Two layers, both plain C (pointers, sizes, enums; no C++ or torch types):
+ *
+ *  1. amcu_* kernel launchers. Each is the CUDA drop-in for one CPU kernel (or
+ *     one kernel the reference declares but has not written) of the reference
+ *     engine's dispatch surface. Launchers are asynchronous on the given stream
+ *     (a cudaStream_t passed as void*, NULL = legacy default stream), validate
+ *     their arguments on the host and return an am_status_code. All tensor
+ *     pointers are DEVICE pointers unless the field says otherwise. On failure
+ *     amcu_last_error() returns a message for the calling thread.
+ *
+ *  2. am_* session API: the engine-level ABI the reference's product spec
+ *     defines (runtime -> model -> session -> generate), run on one B200 (or
+ *     one tensor-parallel rank of several). Host buffers in, host buffers out.
+ *
+ * Status codes, error objects and the argument-struct style are those of the
+ * reference C ABI (include/c_api.h:55-88) and its SDK launchers
+ * (include/aethermind/backend/cpu/kernels/rmsnorm/cpu_rmsnorm_kernel.h:13-53).
+ */
+#ifndef AETHERMIND_B200_H
+#define AETHERMIND_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Status and errors -- same numeric values as the reference's               */
+/* am_status_code (include/c_api.h:55-74), so callers can share handling.     */
+/* ------------------------------------------------------------------------ */
+#ifndef AETHERMIND_C_API_H
+typedef enum am_status_code {
+    AM_STATUS_OK = 0,
+    AM_STATUS_CANCELLED,
+    AM_STATUS_UNKNOWN,
+    AM_STATUS_INVALID_ARGUMENT,
+    AM_STATUS_DEADLINE_EXCEEDED,
+    AM_STATUS_NOT_FOUND,
+    AM_STATUS_ALREADY_EXISTS,
+    AM_STATUS_PERMISSION_DENIED,
+    AM_STATUS_RESOURCE_EXHAUSTED,
+    AM_STATUS_FAILED_PRECONDITION,
+    AM_STATUS_ABORTED,
+    AM_STATUS_OUT_OF_RANGE,
+    AM_STATUS_UNIMPLEMENTED,
+    AM_STATUS_INTERNAL,
+    AM_STATUS_UNAVAILABLE,
+    AM_STATUS_DATA_LOSS,
+    AM_STATUS_OVERFLOW,
+    AM_STATUS_UNAUTHENTICATED
+} am_status_code;
+typedef void* am_error_handle;
+/* Replaces am_error_create/destroy/code/message (include/c_api.h:82-88). */
+am_error_handle am_error_create(am_status_code code, const char* message);
+void am_error_destroy(am_error_handle error);
+am_status_code am_error_code(am_error_handle error);
+const char* am_error_message(am_error_handle error);
+#endif
+
+/* Message of the last failing amcu_* / am_* call on this thread ("" if none). */
+const char* amcu_last_error(void);
+/* Library version string and the CUDA arch it was built for ("sm_100a"). */
+const char* amcu_version(void);
+
+/* Element types (subset of the reference DataType used on the path). */
+typedef enum amcu_dtype {
+    AMCU_F32 = 0,
+    AMCU_BF16 = 1,
+    AMCU_F16 = 2,
+    AMCU_I8 = 3,
+    AMCU_I4 = 4, /* two values per byte */
+    AMCU_I32 = 5,
+    AMCU_I64 = 6,
+    AMCU_U32 = 7
+} amcu_dtype;
+
+/* Weight formats (reference WeightFormat, include/aethermind/backend/kernel_selector.h:25-30). */
+typedef enum amcu_weight_format {
+    AMCU_WFMT_PLAIN = 0,   /* dense weights in the activation dtype, [N, K] row-major */
+    AMCU_WFMT_INT8 = 2,    /* int8 per-output-channel symmetric, fp32 scale [N] */
+    AMCU_WFMT_INT4 = 3     /* int4 group-wise symmetric, fp16 scale per (n, group of 128 along K) */
+} amcu_weight_format;
+
+/* ------------------------------------------------------------------------ */
+/* Weight prepacking (replaces CpuWeightPrepacker::Pack,                      */
+/* src/backend/cpu/cpu_weight_prepacker.cpp:88-119, a memcpy there).          */
+/*                                                                            */
+/* Canonical formats (what callers hand in):                                  */
+/*   INT8: int8 q[N][K], float s[N]                                           */
+/*   INT4: uint8 b[N][K/2] -- low nibble = even k, high nibble = odd k, two's */
+/*         complement in [-8, 7]; uint16 (fp16 bits) s[N][K/128]             */
+/*   PLAIN: act-dtype w[N][K]                                                 */
+/* Device formats (what the GEMV/GEMM kernels read) are opaque; their sizes  */
+/* come from amcu_packed_weight_bytes. Packing is exact: amcu_unpack_weight   */
+/* returns the canonical bytes bit for bit.                                   */
+/* ------------------------------------------------------------------------ */
+typedef struct AmcuWeight {
+    int32_t format;       /* amcu_weight_format */
+    int32_t dtype;        /* PLAIN: element dtype (AMCU_F32 / AMCU_BF16) */
+    int64_t n;            /* output features (rows) */
+    int64_t k;            /* input features */
+    int64_t group;        /* INT4 group size along K (128); ignored otherwise */
+    const void* data;     /* device-format weights */
+    const void* scales;   /* device-format scales (INT8/INT4) */
+    int32_t gate_up_interleaved; /* 1: rows are [gate;up] interleaved by amcu_prepack_gate_up */
+} AmcuWeight;
+
+/* Bytes of the device-format weight / scale buffers. */
+int64_t amcu_packed_weight_bytes(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group);
+int64_t amcu_packed_scale_bytes(int32_t format, int64_t n, int64_t k, int64_t group);
+/* canonical (device pointers) -> device format. */
+am_status_code amcu_prepack_weight(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group,
+                                   const void* q_canonical, const void* s_canonical,
+                                   void* q_packed, void* s_packed, void* stream);
+/* device format -> canonical (for round-trip checks and checkpoint export). */
+am_status_code amcu_unpack_weight(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group,
+                                  const void* q_packed, const void* s_packed,
+                                  void* q_canonical, void* s_canonical, void* stream);
+/* Fused gate/up weight for the SwiGLU MLP: packs gate[I][K] and up[I][K]
+ * (canonical, same format) into one [2I][K] device weight whose GEMV/GEMM
+ * epilogue emits silu(gate)*up directly. I must be a multiple of 8. */
+am_status_code amcu_prepack_gate_up(int32_t format, int32_t dtype, int64_t inter, int64_t k, int64_t group,
+                                    const void* gate_q, const void* gate_s,
+                                    const void* up_q, const void* up_s,
+                                    void* q_packed, void* s_packed, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Synthetic weights: seeded integer-hash generators, bit-identical to the    */
+/* CPU oracle's restatement; canonical formats as above.                      */
+/* ------------------------------------------------------------------------ */
+am_status_code amcu_synth_w4(uint64_t seed, uint64_t stream_id, int64_t n, int64_t k, float base_scale,
+                             void* q_canonical, void* s_canonical, void* stream);
+am_status_code amcu_synth_w8(uint64_t seed, uint64_t stream_id, int64_t n, int64_t k, float base_scale,
+                             void* q_canonical, void* s_canonical, void* stream);
+am_status_code amcu_synth_uniform_bf16(uint64_t seed, uint64_t stream_id, int64_t count, float amplitude,
+                                       void* out, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* RMSNorm (+ optional fused residual add).                                   */
+/* Replaces LaunchRmsNorm(const RmsNormArgs&)                                 */
+/* (include/aethermind/backend/cpu/kernels/rmsnorm/cpu_rmsnorm_kernel.h:53)   */
+/* and the Add that precedes it when residual != NULL                         */
+/* (src/backend/cpu/kernels/add/add_scalar.cpp:56-65):                        */
+/*   h = residual ? round(input + residual) : input ; residual_out <- h        */
+/*   output = round(h * (mean(h^2) + eps)^-1/2 * weight)                      */
+/* rows == 0 returns OK without touching memory (rmsnorm_entry.cpp:98-103).   */
+/* ------------------------------------------------------------------------ */
+typedef struct AmcuRmsNormArgs {
+    const void* input;
+    const void* weight;
+    void* output;
+    const void* residual;   /* optional */
+    void* residual_out;     /* required when residual != NULL; may alias input */
+    int64_t rows;
+    int64_t hidden;
+    int64_t input_row_stride;   /* elements; 0 = hidden */
+    int64_t output_row_stride;  /* elements; 0 = hidden */
+    float eps;
+    int32_t dtype;              /* AMCU_F32 or AMCU_BF16 (input/output/weight) */
+} AmcuRmsNormArgs;
+am_status_code amcu_rmsnorm(const AmcuRmsNormArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Linear: y[m, n] = sum_k x[m, k] * W[n, k]  (W [N=out, K=in], reference     */
+/* LinearOp include/aethermind/operators/linear_op.h:87-91). No reference     */
+/* kernel exists (LinearOp resolves NOT_FOUND); these are new.                */
+/* ------------------------------------------------------------------------ */
+typedef enum amcu_epilogue {
+    AMCU_EPI_STORE = 0,        /* y = round(acc) */
+    AMCU_EPI_RESIDUAL_ADD = 1, /* y = round(residual + round(acc)); residual may alias y */
+    AMCU_EPI_SILU_MUL = 2      /* gate/up interleaved weight: y[m, i] = round(silu(round(g)) * round(u)) */
+} amcu_epilogue;
+
+typedef struct AmcuLinearArgs {
+    const void* x;          /* [m, k] act dtype, row stride x_stride */
+    AmcuWeight w;
+    void* y;                /* [m, n] (SILU_MUL: [m, n/2]), row stride y_stride */
+    const void* residual;   /* EPI_RESIDUAL_ADD only, row stride y_stride */
+    int64_t m;
+    int64_t x_stride;       /* elements; 0 = k */
+    int64_t y_stride;       /* elements; 0 = n (or n/2 for SILU_MUL) */
+    int32_t act_dtype;      /* AMCU_BF16 (quantized formats) or the plain weight dtype */
+    int32_t epilogue;       /* amcu_epilogue */
+    void* workspace;        /* device scratch (prefill GEMM); may be NULL for m <= 8 */
+    size_t workspace_size;
+} AmcuLinearArgs;
+/* Dispatches on m: GEMV (m <= 8) or the tensor-core GEMM (m > 8). */
+am_status_code amcu_linear(const AmcuLinearArgs* args, void* stream);
+/* Bytes of workspace amcu_linear needs for these arguments (0 if none). */
+size_t amcu_linear_workspace_bytes(const AmcuLinearArgs* args);
+/* Decode GEMVs (m <= 8): W8 per-channel and W4 group-128. */
+am_status_code amcu_gemv_w8(const AmcuLinearArgs* args, void* stream);
+am_status_code amcu_gemv_w4g128(const AmcuLinearArgs* args, void* stream);
+/* Prefill GEMMs (any m >= 1): dequant-to-bf16 tensor-core GEMM. */
+am_status_code amcu_gemm_w8_prefill(const AmcuLinearArgs* args, void* stream);
+am_status_code amcu_gemm_w4g128_prefill(const AmcuLinearArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* RoPE + KV-cache write (replaces the RoPE and KVCacheUpdate nodes,          */
+/* src/operators/rope_op.cpp:202-223, src/operators/kvcache_update_op.cpp).   */
+/* Split-half rotation with inv_freq[i] = theta^(-2i/d) and angles in double  */
+/* (reference RoPE design doc). Row r belongs to sequence b = r / rows_per_seq */
+/* at position seq_pos[b] + r % rows_per_seq. q is rotated in place; k is     */
+/* rotated and, with v, stored at cache[b][kv_head][pos][:]                   */
+/* (layout of src/execution/kv_cache_view.cpp:41-75 with a leading slot axis).*/
+/* ------------------------------------------------------------------------ */
+typedef struct AmcuRopeKvArgs {
+    void* q;                 /* [rows, n_q_heads * head_dim] (in place) */
+    const void* k;           /* [rows, n_kv_heads * head_dim] */
+    const void* v;           /* [rows, n_kv_heads * head_dim] */
+    int64_t q_stride, k_stride, v_stride;   /* row strides in elements */
+    void* k_cache;           /* this layer's K plane: [slots][n_kv][capacity][head_dim] */
+    void* v_cache;
+    int64_t slot_stride;     /* elements between slots (n_kv * capacity * head_dim if 0) */
+    int64_t capacity;        /* max tokens per slot */
+    const int32_t* seq_pos;  /* device [n_seq]: position of each sequence's first row */
+    int64_t rows;
+    int64_t rows_per_seq;
+    int64_t n_q_heads, n_kv_heads, head_dim;
+    double theta;
+    int32_t dtype;           /* AMCU_F32 / AMCU_BF16 (activations and cache) */
+    int32_t* status;         /* optional device word: set to AM_STATUS_OUT_OF_RANGE on a position >= capacity */
+} AmcuRopeKvArgs;
+am_status_code amcu_rope_kv_write(const AmcuRopeKvArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* GQA attention over the static KV cache (reference InferAttention,          */
+/* src/operators/attention_op.cpp:65-169): causal scaled dot-product,         */
+/* kv_head = q_head / (n_q/n_kv). Query row r of sequence b sits at position  */
+/* seq_pos[b] + r % rows_per_seq and sees cache positions [0, that position]. */
+/* Decode (rows_per_seq == 1): split-K over the sequence with a combine step; */
+/* needs workspace (amcu_attention_workspace_bytes). Prefill: flash tiles.    */
+/* ------------------------------------------------------------------------ */
+typedef struct AmcuAttentionArgs {
+    const void* q;           /* [rows, n_q_heads * head_dim] */
+    int64_t q_stride;
+    const void* k_cache;     /* [slots][n_kv][capacity][head_dim] */
+    const void* v_cache;
+    int64_t slot_stride;
+    int64_t capacity;
+    const int32_t* seq_pos;  /* device [n_seq] */
+    void* out;               /* [rows, n_q_heads * head_dim] */
+    int64_t out_stride;
+    int64_t rows;
+    int64_t rows_per_seq;
+    int64_t n_q_heads, n_kv_heads, head_dim;
+    int32_t dtype;           /* AMCU_F32 / AMCU_BF16 */
+    int32_t num_splits;      /* decode only: 0 = choose from max_context */
+    int64_t max_context;     /* upper bound on position+1 (sizes the split grid) */
+    void* workspace;
+    size_t workspace_size;
+} AmcuAttentionArgs;
+size_t amcu_attention_workspace_bytes(const AmcuAttentionArgs* args);
+am_status_code amcu_attn_decode(const AmcuAttentionArgs* args, void* stream);
+am_status_code amcu_attn_prefill(const AmcuAttentionArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* SiLU-Mul: out = round(silu(gate) * up), sign-branched fp32 SiLU            */
+/* (src/graph/optimization/const_eval_silu_mul.cpp:18-33).                   */
+/* ------------------------------------------------------------------------ */
+am_status_code amcu_silu_mul(const void* gate, const void* up, void* out, int64_t count,
+                             int32_t dtype, void* stream);
+/* Residual add: out = round(a + b) (src/backend/cpu/kernels/add/add_scalar.cpp:56-65). */
+am_status_code amcu_add(const void* a, const void* b, void* out, int64_t count, int32_t dtype,
+                        void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Greedy argmax over the last axis (src/operators/argmax_op.cpp:6-45);      */
+/* ties resolve to the lowest index. out_index: int64 [rows].                */
+/* Optional out_gap: float [rows] = max - second max (near-tie detection).   */
+/* ------------------------------------------------------------------------ */
+am_status_code amcu_argmax(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                           int32_t dtype, int64_t* out_index, float* out_gap, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Embedding gather (src/backend/cpu/kernels/embedding/embedding_entry.cpp:  */
+/* 32-126). ids: int32/int64/uint32 [count]. table: act-dtype [vocab, hidden] */
+/* or INT8 rows + fp32 row scales (tied int8 lm_head), dequantized to bf16.  */
+/* A bad id leaves its row zero and, if status != NULL, sets *status (device) */
+/* to AM_STATUS_OUT_OF_RANGE.                                                 */
+/* ------------------------------------------------------------------------ */
+typedef struct AmcuEmbeddingArgs {
+    const void* ids;
+    int32_t id_dtype;        /* AMCU_I32 / AMCU_I64 / AMCU_U32 */
+    int64_t count;
+    const void* table;
+    const float* row_scales; /* non-NULL: table is int8 rows */
+    int64_t vocab, hidden;
+    void* out;               /* [count, hidden] */
+    int32_t dtype;           /* output dtype AMCU_F32 / AMCU_BF16 */
+    int32_t* status;
+} AmcuEmbeddingArgs;
+am_status_code amcu_embedding(const AmcuEmbeddingArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Session API (reference product spec: docs/products/aethermind_prd.md:     */
+/* 296-320; the reference has not implemented it).                          */
+/* ------------------------------------------------------------------------ */
+typedef struct am_runtime_s* am_runtime_t;
+typedef struct am_model_s* am_model_t;
+typedef struct am_session_s* am_session_t;
+typedef am_error_handle am_error_t;
+
+typedef struct am_config_t {
+    int32_t device_id;       /* CUDA device of this process */
+    int32_t tp_rank;         /* tensor-parallel rank (0 for 1 GPU) */
+    int32_t tp_size;         /* tensor-parallel world size (1 for 1 GPU) */
+    const void* nccl_unique_id;  /* 128-byte ncclUniqueId shared by all ranks (tp_size > 1) */
+} am_config_t;
+
+typedef struct am_model_config_t {
+    int64_t vocab, hidden, layers, n_q_heads, n_kv_heads, head_dim, inter;
+    float rms_eps;
+    double rope_theta;
+    int32_t tied_embeddings;
+    int32_t act_dtype;       /* AMCU_F32 (plain fp32 weights) or AMCU_BF16 */
+    int32_t weight_format;   /* amcu_weight_format */
+    int64_t group_size;      /* 128 for INT4 */
+    int64_t max_seq;         /* static KV capacity per sequence */
+    int64_t max_batch;       /* sequences per generate call (KV slots) */
+} am_model_config_t;
+
+typedef struct am_session_config_t {
+    int64_t max_new_tokens;
+    int32_t use_cuda_graph;  /* 1: decode steps replay a captured CUDA graph */
+} am_session_config_t;
+
+am_runtime_t am_runtime_create(const am_config_t* config);
+void am_runtime_destroy(am_runtime_t runtime);
+
+/* Weights from an on-disk checkpoint. Not supported yet: returns NULL with
+ * AM_STATUS_UNIMPLEMENTED (synthetic and host-provided weights only). */
+am_model_t am_model_load(am_runtime_t runtime, const char* path, am_error_t* error);
+/* Creates a model with device storage for every weight (uninitialised). */
+am_model_t am_model_create(am_runtime_t runtime, const am_model_config_t* config, am_error_t* error);
+/* Fills every weight from the seeded synthetic generator on the device. */
+am_status_code am_model_init_synthetic(am_model_t model, uint64_t seed);
+/* Sets one weight from HOST memory in canonical format. Names:
+ * "embed" [vocab, hidden]; "final_norm" [hidden]; "lm_head" (untied);
+ * "layers.<i>.{attn_norm,mlp_norm}" [hidden];
+ * "layers.<i>.{wq,wk,wv,wo,wg,wu,wd}" -- data = q / plain weights, scales = scales.
+ * For tp_size > 1 pass the FULL tensor; the rank keeps its shard. */
+am_status_code am_model_set_weight(am_model_t model, const char* name, const void* data,
+                                   const void* scales);
+void am_model_unload(am_model_t model);
+
+am_session_t am_session_create(am_model_t model, const am_session_config_t* config);
+void am_session_destroy(am_session_t session);
+/* Greedy generation for one sequence: prefill input_tokens, then decode until
+ * output_capacity tokens (or the session's max_new_tokens). Host buffers. */
+int am_session_generate(am_session_t session, const uint32_t* input_tokens, size_t input_len,
+                        uint32_t* output_tokens, size_t output_capacity, size_t* output_len,
+                        am_error_t* error);
+/* Batched variant: batch sequences of equal prompt length, row-major
+ * input [batch][input_len], output [batch][output_capacity]. */
+int am_session_generate_batch(am_session_t session, const uint32_t* input_tokens, size_t batch,
+                              size_t input_len, uint32_t* output_tokens, size_t output_capacity,
+                              size_t* output_len, am_error_t* error);
+/* Device-timed phases of the last generate call (CUDA events), in ms. */
+am_status_code am_session_last_timing(am_session_t session, double* prefill_ms, double* decode_ms,
+                                      int64_t* decode_steps);
+/* Optional: logits top-1/top-2 gap per generated token of the last call
+ * (host float [batch][n]) for near-tie diagnostics. */
+am_status_code am_session_last_gaps(am_session_t session, float* gaps, size_t capacity);
+
+/* Tensor parallelism: rank 0 creates the 128-byte NCCL unique id and shares it
+ * with the other ranks (any transport) before am_runtime_create. */
+am_status_code am_nccl_get_unique_id(void* out128);
+/* Message of the last failing am_* session call on this thread. */
+const char* am_last_error(void);
+/* Diagnostics: number of registered CUDA kernels, and the resolved kernel of
+ * every step of a plan (phase 0 = prefill, 1 = decode) as text lines. */
+int64_t am_debug_registry_size(void);
+am_status_code am_debug_plan_steps(am_session_t session, int32_t phase, int64_t batch, int64_t rows_per_seq,
+                                   char* buf, size_t capacity);
+/* Kernel resolution through the CUDA backend's registry (no GPU needed):
+ * op = reference OpType value, act/weight = amcu_dtype, format = reference
+ * WeightFormat value (0 plain, 2 int8, 3 int4), phase 0 prefill / 1 decode /
+ * 2 both. Writes the resolved kernel name; NOT_FOUND when none matches. */
+am_status_code am_debug_resolve_kernel(int32_t op, int32_t act, int32_t weight, int32_t format, int32_t phase,
+                                       char* name, size_t capacity);
+/* KV layout offset (bytes) and bytes per plane exactly as the HBM KV manager
+ * computes them (layout only, nothing is allocated). */
+am_status_code am_debug_kv_offset(uint64_t layers, uint64_t kv_heads, uint64_t max_tokens, uint64_t head_dim,
+                                  int32_t dtype, uint64_t slots, uint64_t layer, uint64_t kv_head, uint64_t pos,
+                                  uint64_t dim, uint64_t slot, uint64_t* offset, uint64_t* bytes_per_plane);
+/* Session reservation contract of the KV manager (capacity checks only). */
+am_status_code am_debug_kv_reserve(uint64_t max_tokens, uint64_t prompt_len, uint64_t max_new);
+
+#ifdef __cplusplus
+}
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#endif

@@ -1,0 +1,107 @@
+"""End-to-end greedy generation through the am_* session ABI vs the CPU oracle.
+
+Greedy token ids must match the oracle except at documented near-ties: the
+comparison walks the sequence and, at the first mismatch, requires the
+oracle's top-1/top-2 logit gap there to be below the near-tie threshold
+(1e-4 for fp32 models, 0.05 for bf16 models, whose logits carry bf16
+rounding). After a legitimate near-tie flip the sequences diverge, so the
+remainder is not compared.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _compare(got, ref, gaps, tie):
+    for i, (a, b) in enumerate(zip(got, ref)):
+        if a != b:
+            assert gaps[i] < tie, f"token {i}: {a} != {b} with oracle gap {gaps[i]:.4g} >= {tie}"
+            return i
+    return len(ref)
+
+
+@pytest.fixture(scope="module")
+def sess_mod(built_lib):
+    from aethermind_b200 import session
+    return session
+
+
+@pytest.fixture(scope="module")
+def rt(sess_mod):
+    return sess_mod.Runtime(0)
+
+
+def test_tiny_f32_model_matches_oracle(sess_mod, rt, oracle_lib):
+    from tests.model_fixtures import load_tiny_into_engine, tiny_oracle_model, tiny_prompt, tiny_weights
+    cfg = sess_mod.TINY_F32
+    w = tiny_weights(cfg)
+    m = sess_mod.Model(rt, cfg)
+    load_tiny_into_engine(m, w)
+    s = sess_mod.Session(m)
+    prompt = tiny_prompt(cfg)
+    got = s.generate(prompt, 32)
+    ref, gaps = tiny_oracle_model(cfg, w).generate(prompt.astype(np.int64), 32)
+    n = _compare(got.tolist(), ref.tolist(), gaps, 1e-4)
+    assert n >= 16, f"only {n} tokens matched before a near-tie"
+    # CUDA graph replay and eager execution produce identical tokens
+    s2 = sess_mod.Session(m, use_cuda_graph=False)
+    np.testing.assert_array_equal(s2.generate(prompt, 32), got)
+    # a second call on the same session reuses the captured graph
+    np.testing.assert_array_equal(s.generate(prompt, 32), got)
+
+
+def _small(cfg_name, sess_mod, layers=2):
+    import dataclasses
+    base = getattr(sess_mod, cfg_name)
+    return dataclasses.replace(base, layers=layers, max_seq=256, max_batch=2)
+
+
+@pytest.mark.parametrize("cfg_name", ["LLAMA_8B_W4", "LLAMA_1B_W8"])
+def test_quantized_model_matches_oracle(sess_mod, rt, oracle_lib, cfg_name):
+    cfg = _small(cfg_name, sess_mod)
+    m = sess_mod.Model(rt, cfg)
+    m.init_synthetic(seed=0)
+    s = sess_mod.Session(m)
+    prompt = np.random.default_rng(5).integers(0, cfg.vocab, 16).astype(np.uint32)
+    got = s.generate(prompt, 8)
+    om = oracle_lib.synthetic_oracle_model(cfg, seed=0)
+    ref, gaps = om.generate(prompt.astype(np.int64), 8)
+    n = _compare(got.tolist(), ref.tolist(), gaps, 0.05)
+    assert n >= 4
+    # batch of 2 equals two single runs (per-row math is independent of the batch)
+    p2 = np.stack([prompt, np.random.default_rng(6).integers(0, cfg.vocab, 16).astype(np.uint32)])
+    gb = s.generate(p2, 8)
+    np.testing.assert_array_equal(gb[0], got)
+    np.testing.assert_array_equal(gb[1], s.generate(p2[1], 8))
+
+
+def test_plan_resolves_phase_kernels(sess_mod, rt):
+    cfg = _small("LLAMA_8B_W4", sess_mod, layers=1)
+    m = sess_mod.Model(rt, cfg)
+    m.init_synthetic(0)
+    s = sess_mod.Session(m)
+    dec = s.plan_steps(1, 1, 1)
+    pre = s.plan_steps(0, 1, 16)
+    assert any("GemvW4G128_CUDA_Decode" in l for l in dec)
+    assert any("AttnDecodeSplitK" in l for l in dec)
+    assert any("GemmW4G128_CUDA_Prefill" in l for l in pre)
+    assert any("AttnPrefill" in l for l in pre)
+    names = [l.split()[0] for l in dec]
+    assert names[0] == "embedding" and names[-1] == "argmax"
+
+
+def test_session_errors(sess_mod, rt):
+    from aethermind_b200._lib import AmError
+    cfg = _small("LLAMA_8B_W4", sess_mod, layers=1)
+    m = sess_mod.Model(rt, cfg)
+    m.init_synthetic(0)
+    s = sess_mod.Session(m)
+    with pytest.raises(AmError) as e:
+        s.generate(np.zeros(250, np.uint32), 10)  # 250 + 10 > max_seq 256
+    assert e.value.code == 11
+    with pytest.raises(AmError) as e:
+        s.generate(np.array([cfg.vocab], np.uint32), 2)
+    assert e.value.code == 11
+    # the session stays usable after errors
+    assert s.generate(np.array([1, 2, 3], np.uint32), 2).shape == (2,)

@@ -1,0 +1,331 @@
+"""Per-op parity of the CUDA kernels (through the C ABI) against the CPU oracle.
+
+Tolerances: integer/byte work (synthetic weights, packing, argmax indices,
+KV addressing) is bit-exact; bf16 outputs are compared with rtol 1e-2 (the
+north-star bf16 tolerance) and fp32 outputs with rtol 1e-4 (plus a small atol
+for values near zero).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+BF_RTOL, BF_ATOL = 1e-2, 1e-2
+F32_RTOL = 1e-4
+
+
+@pytest.fixture(scope="module")
+def ops(built_lib):
+    from aethermind_b200 import ops as O
+    return O
+
+
+@pytest.fixture(scope="module")
+def orc(oracle_lib):
+    return oracle_lib
+
+
+@pytest.fixture(scope="module")
+def gold():
+    from pathlib import Path
+    return np.load(Path(__file__).parent / "golden" / "ref_kernels.npz")
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def bf16_dev(a_f32):
+    return torch.from_numpy(np.ascontiguousarray(a_f32, np.float32)).cuda().to(torch.bfloat16)
+
+
+def to_np(t):
+    return t.float().cpu().numpy() if t.dtype == torch.bfloat16 else t.cpu().numpy()
+
+
+# ------------------------------------------------------------- weights
+def test_synth_bit_exact_vs_oracle(ops, orc):
+    q, s = ops.synth_w4(11, 9, 64, 512, orc.W4_BASE)
+    rq, rs = orc.synth_w4(11, 9, 64, 512, orc.W4_BASE)
+    np.testing.assert_array_equal(q.cpu().numpy(), rq)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16), rs)
+    q8, s8 = ops.synth_w8(11, 9, 32, 256, orc.W8_BASE)
+    rq8, rs8 = orc.synth_w8(11, 9, 32, 256, orc.W8_BASE)
+    np.testing.assert_array_equal(q8.cpu().numpy(), rq8)
+    np.testing.assert_array_equal(s8.cpu().numpy(), rs8)
+    e = ops.synth_uniform_bf16(11, 1, 4096, orc.EMBED_AMP)
+    np.testing.assert_array_equal(e.cpu().view(torch.int16).numpy().view(np.uint16),
+                                  orc.synth_uniform_bf16(11, 1, 4096, orc.EMBED_AMP))
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
+def test_prepack_roundtrip_bit_exact(ops, fmt):
+    from aethermind_b200 import _lib as L
+    n, k = 96, 1024
+    if fmt == "int4":
+        q, s = ops.synth_w4(3, 1, n, k, 0.01)
+        pw = ops.prepack(L.WFMT_INT4, q, s, n, k)
+    else:
+        q, s = ops.synth_w8(3, 1, n, k, 0.01)
+        pw = ops.prepack(L.WFMT_INT8, q, s, n, k)
+    q2, s2 = ops.unpack(pw)
+    assert torch.equal(q2.view(torch.uint8).flatten(), q.view(torch.uint8).flatten())
+    assert torch.equal(s2.flatten().view(torch.uint8), s.flatten().view(torch.uint8))
+
+
+# ------------------------------------------------------------- rmsnorm
+def test_rmsnorm_f32_matches_reference_kernels(ops, gold):
+    for name in ("small", "h4096"):
+        x, w = gold[f"rmsnorm_{name}_x"], gold[f"rmsnorm_{name}_w"]
+        y = ops.rmsnorm(dev(x), dev(w), 1e-5)
+        np.testing.assert_allclose(to_np(y), gold[f"rmsnorm_{name}_scalar"], rtol=F32_RTOL, atol=1e-6)
+    y = ops.rmsnorm(dev(np.array([[1, 2, 3, 4]], np.float32)), dev(np.ones(4, np.float32)), 1e-5)
+    np.testing.assert_allclose(to_np(y)[0], [0.365148, 0.730297, 1.095445, 1.460593], atol=1e-5)
+
+
+@pytest.mark.parametrize("m", [1, 8, 64, 512])
+def test_rmsnorm_bf16_fused_residual(ops, orc, m):
+    rng = np.random.default_rng(m)
+    x = orc.bf16_round(rng.normal(0, 1, (m, 4096)).astype(np.float32))
+    r = orc.bf16_round(rng.normal(0, 1, (m, 4096)).astype(np.float32))
+    w = orc.bf16_round(rng.uniform(0.5, 1.5, 4096).astype(np.float32))
+    y, h = ops.rmsnorm(bf16_dev(x), bf16_dev(w), 1e-5, residual=bf16_dev(r))
+    h_ref = orc.bf16_round(x + r)
+    np.testing.assert_array_equal(to_np(h), h_ref)
+    np.testing.assert_allclose(to_np(y), orc.rmsnorm(h_ref, w, 1e-5, bf=True), rtol=BF_RTOL, atol=BF_ATOL)
+
+
+def test_rmsnorm_empty_rows_is_ok(ops):
+    x = torch.empty(0, 64, device="cuda", dtype=torch.float32)
+    y = ops.rmsnorm(x, torch.ones(64, device="cuda"), 1e-5)
+    assert y.shape == (0, 64)
+
+
+# ------------------------------------------------------------- linear
+def _w(ops, orc, fmt, n, k, seed=5):
+    from aethermind_b200 import _lib as L
+    if fmt == "int4":
+        q, s = ops.synth_w4(seed, 2, n, k, orc.W4_BASE)
+        return ops.prepack(L.WFMT_INT4, q, s, n, k), (q.cpu().numpy(), s.cpu().numpy().view(np.uint16))
+    q, s = ops.synth_w8(seed, 2, n, k, orc.W8_BASE)
+    return ops.prepack(L.WFMT_INT8, q, s, n, k), (q.cpu().numpy(), s.cpu().numpy())
+
+
+def _oracle_linear(orc, fmt, x, host):
+    return orc.linear_w4(x, *host) if fmt == "int4" else orc.linear_w8(x, *host)
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
+@pytest.mark.parametrize("m", [1, 8])
+@pytest.mark.parametrize("n", [4096, 14336])
+def test_gemv_matches_oracle(ops, orc, fmt, m, n):
+    k = 4096
+    pw, host = _w(ops, orc, fmt, n, k)
+    x = orc.bf16_round(np.random.default_rng(m).normal(0, 1, (m, k)).astype(np.float32))
+    entry = "amcu_gemv_w4g128" if fmt == "int4" else "amcu_gemv_w8"
+    y = ops.linear(bf16_dev(x), pw, entry=entry)
+    np.testing.assert_allclose(to_np(y), _oracle_linear(orc, fmt, x, host), rtol=BF_RTOL, atol=BF_ATOL)
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
+@pytest.mark.parametrize("m", [64, 512])
+def test_prefill_gemm_matches_torch_fp32(ops, orc, fmt, m):
+    """Large-m GEMM against a torch fp32 matmul of the unpacked weights."""
+    n, k = 4096, 4096
+    pw, host = _w(ops, orc, fmt, n, k)
+    x = orc.bf16_round(np.random.default_rng(m).normal(0, 1, (m, k)).astype(np.float32))
+    entry = "amcu_gemm_w4g128_prefill" if fmt == "int4" else "amcu_gemm_w8_prefill"
+    y = ops.linear(bf16_dev(x), pw, entry=entry)
+    if fmt == "int4":
+        q = torch.from_numpy(orc.unpack_w4(host[0], n, k)).cuda().float()
+        s = torch.from_numpy(host[1].view(np.float16)).cuda().float().repeat_interleave(128, dim=1)
+        wd = q * s
+    else:
+        wd = torch.from_numpy(host[0]).cuda().float() * torch.from_numpy(host[1]).cuda()[:, None]
+    ref = dev(x) @ wd.T
+    torch.testing.assert_close(y.float(), ref, rtol=BF_RTOL, atol=5e-2)
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
+def test_linear_residual_and_silu_epilogues(ops, orc, fmt):
+    from aethermind_b200 import _lib as L
+    m, k, inter, n = 4, 4096, 1024, 2048
+    rng = np.random.default_rng(2)
+    x = orc.bf16_round(rng.normal(0, 1, (m, k)).astype(np.float32))
+    res = orc.bf16_round(rng.normal(0, 1, (m, n)).astype(np.float32))
+    pw, host = _w(ops, orc, fmt, n, k)
+    xr = bf16_dev(res)
+    y = ops.linear(bf16_dev(x), pw, epilogue=L.EPI_RESIDUAL_ADD, residual=xr, out=xr)  # in place
+    ref = orc.bf16_round(res + _oracle_linear(orc, fmt, x, host))
+    np.testing.assert_allclose(to_np(y), ref, rtol=BF_RTOL, atol=BF_ATOL)
+    # gate/up interleaved + SiLU-Mul
+    if fmt == "int4":
+        gq, gs = ops.synth_w4(8, 1, inter, k, orc.W4_BASE)
+        uq, us = ops.synth_w4(8, 2, inter, k, orc.W4_BASE)
+        gu = ops.prepack_gate_up(L.WFMT_INT4, gq, gs, uq, us, inter, k)
+        g = orc.linear_w4(x, gq.cpu().numpy(), gs.cpu().numpy().view(np.uint16))
+        u = orc.linear_w4(x, uq.cpu().numpy(), us.cpu().numpy().view(np.uint16))
+    else:
+        gq, gs = ops.synth_w8(8, 1, inter, k, orc.W8_BASE)
+        uq, us = ops.synth_w8(8, 2, inter, k, orc.W8_BASE)
+        gu = ops.prepack_gate_up(L.WFMT_INT8, gq, gs, uq, us, inter, k)
+        g = orc.linear_w8(x, gq.cpu().numpy(), gs.cpu().numpy())
+        u = orc.linear_w8(x, uq.cpu().numpy(), us.cpu().numpy())
+    y = ops.linear(bf16_dev(x), gu, epilogue=L.EPI_SILU_MUL)
+    np.testing.assert_allclose(to_np(y), orc.silu_mul(g, u, bf=True), rtol=BF_RTOL, atol=BF_ATOL)
+    # the same weights through the prefill GEMM path (m = 64)
+    x64 = orc.bf16_round(rng.normal(0, 1, (64, k)).astype(np.float32))
+    y64 = ops.linear(bf16_dev(x64), gu, epilogue=L.EPI_SILU_MUL)
+    g64 = _oracle_linear(orc, fmt, x64, (gq.cpu().numpy(), gs.cpu().numpy().view(np.uint16) if fmt == "int4" else gs.cpu().numpy()))
+    u64 = _oracle_linear(orc, fmt, x64, (uq.cpu().numpy(), us.cpu().numpy().view(np.uint16) if fmt == "int4" else us.cpu().numpy()))
+    np.testing.assert_allclose(to_np(y64), orc.silu_mul(g64, u64, bf=True), rtol=BF_RTOL, atol=BF_ATOL)
+
+
+def test_plain_f32_linear(ops, orc):
+    from aethermind_b200 import _lib as L
+    rng = np.random.default_rng(4)
+    x = rng.normal(0, 1, (16, 256)).astype(np.float32)
+    w = rng.normal(0, 0.02, (688, 256)).astype(np.float32)
+    pw = ops.PackedWeight(L.WFMT_PLAIN, 688, 256, L.F32, 128, dev(w), None)
+    y = ops.linear(dev(x), pw)
+    np.testing.assert_allclose(to_np(y), orc.linear_f32(x, w), rtol=F32_RTOL, atol=1e-6)
+
+
+# ------------------------------------------------------------- rope / kv / attention
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_rope_kv_write_matches_oracle(ops, orc, dtype):
+    nq, nkv, d, theta, M, cap = 32, 8, 128, 500000.0, 5, 64
+    rng = np.random.default_rng(0)
+    q = rng.normal(0, 1, (M, nq * d)).astype(np.float32)
+    k = rng.normal(0, 1, (M, nkv * d)).astype(np.float32)
+    v = rng.normal(0, 1, (M, nkv * d)).astype(np.float32)
+    bf = dtype == "bf16"
+    if bf:
+        q, k, v = orc.bf16_round(q), orc.bf16_round(k), orc.bf16_round(v)
+    mk = bf16_dev if bf else dev
+    qd, kd, vd = mk(q), mk(k), mk(v)
+    tdt = torch.bfloat16 if bf else torch.float32
+    kc = torch.zeros(1, nkv, cap, d, dtype=tdt, device="cuda")
+    vc = torch.zeros_like(kc)
+    seq_pos = torch.tensor([40], dtype=torch.int32, device="cuda")
+    ops.rope_kv_write(qd, kd, vd, kc, vc, seq_pos, M, nq, nkv, d, theta)
+    pos = 40 + np.arange(M)
+    qr = orc.rope(q, pos, nq, d, theta, bf=bf)
+    kr = orc.rope(k, pos, nkv, d, theta, bf=bf)
+    np.testing.assert_array_equal(to_np(qd), qr)
+    kcn = to_np(kc)
+    for i in range(M):
+        np.testing.assert_array_equal(kcn[0, :, 40 + i, :], kr[i].reshape(nkv, d))
+        np.testing.assert_array_equal(to_np(vc)[0, :, 40 + i, :], v[i].reshape(nkv, d))
+    assert not kcn[0, :, :40].any()  # nothing written outside [pos, pos + M)
+
+
+def test_rope_out_of_capacity_sets_status(ops):
+    q = torch.zeros(1, 4 * 64, device="cuda")
+    kv = torch.zeros(1, 2 * 64, device="cuda")
+    kc = torch.zeros(1, 2, 8, 64, device="cuda")
+    vc = torch.zeros_like(kc)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.rope_kv_write(q, kv, kv, kc, vc, torch.tensor([8], dtype=torch.int32, device="cuda"), 1, 4, 2, 64, 1e4,
+                      status=st)
+    assert int(st.item()) == 11 and not kc.any()
+
+
+@pytest.mark.parametrize("L", [512, 2048, 8192])
+def test_attention_decode_matches_oracle(ops, orc, L):
+    nq, nkv, d = 32, 8, 128
+    rng = np.random.default_rng(L)
+    q = orc.bf16_round(rng.normal(0, 1, (1, nq * d)).astype(np.float32))
+    kp = orc.bf16_round(rng.normal(0, 1, (nkv, L, d)).astype(np.float32))
+    vp = orc.bf16_round(rng.normal(0, 1, (nkv, L, d)).astype(np.float32))
+    kc, vc = bf16_dev(kp)[None], bf16_dev(vp)[None]
+    seq_pos = torch.tensor([L - 1], dtype=torch.int32, device="cuda")
+    out = ops.attention(bf16_dev(q), kc, vc, seq_pos, 1, nq, nkv, d, max_context=L)
+    ref = orc.attention(q, kp, vp, L - 1, nq, nkv, d, bf=True)
+    np.testing.assert_allclose(to_np(out), ref, rtol=BF_RTOL, atol=BF_ATOL)
+
+
+def test_attention_decode_batch_slots(ops, orc):
+    nq, nkv, d, cap = 8, 2, 64, 96
+    rng = np.random.default_rng(9)
+    B = 3
+    q = orc.bf16_round(rng.normal(0, 1, (B, nq * d)).astype(np.float32))
+    kp = orc.bf16_round(rng.normal(0, 1, (B, nkv, cap, d)).astype(np.float32))
+    vp = orc.bf16_round(rng.normal(0, 1, (B, nkv, cap, d)).astype(np.float32))
+    pos = np.array([5, 60, 95], np.int32)
+    out = ops.attention(bf16_dev(q), bf16_dev(kp), bf16_dev(vp), dev(pos), 1, nq, nkv, d, max_context=cap)
+    for b in range(B):
+        ref = orc.attention(q[b:b + 1], kp[b], vp[b], int(pos[b]), nq, nkv, d, bf=True)
+        np.testing.assert_allclose(to_np(out)[b:b + 1], ref, rtol=BF_RTOL, atol=BF_ATOL)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_attention_prefill_causal(ops, orc, dtype):
+    nq, nkv, d, M, p0, cap = 32, 8, 128, 48, 16, 128
+    rng = np.random.default_rng(1)
+    bf = dtype == "bf16"
+    rnd = orc.bf16_round if bf else (lambda a: a)
+    q = rnd(rng.normal(0, 1, (M, nq * d)).astype(np.float32))
+    kp = rnd(rng.normal(0, 1, (nkv, cap, d)).astype(np.float32))
+    vp = rnd(rng.normal(0, 1, (nkv, cap, d)).astype(np.float32))
+    mk = bf16_dev if bf else dev
+    out = ops.attention(mk(q), mk(kp)[None], mk(vp)[None], torch.tensor([p0], dtype=torch.int32, device="cuda"),
+                        M, nq, nkv, d, decode=False)
+    ref = orc.attention(q, kp, vp, p0, nq, nkv, d, bf=bf)
+    if bf:
+        np.testing.assert_allclose(to_np(out), ref, rtol=BF_RTOL, atol=BF_ATOL)
+    else:
+        np.testing.assert_allclose(to_np(out), ref, rtol=F32_RTOL, atol=1e-5)
+
+
+# ------------------------------------------------------------- elementwise
+def test_silu_mul_and_add_match_reference_bits(ops, orc, gold):
+    g = torch.from_numpy(gold["silu_g_bf16"].view(np.int16)).cuda().view(torch.bfloat16)
+    u = torch.from_numpy(gold["silu_u_bf16"].view(np.int16)).cuda().view(torch.bfloat16)
+    y = ops.silu_mul(g, u)
+    got = y.view(torch.int16).cpu().numpy().view(np.uint16)
+    # device expf may differ from the host libm in the last fp32 bit: allow 1 bf16 ulp
+    diff = np.abs(got.astype(np.int32) - gold["silu_bf16"].astype(np.int32))
+    assert diff.max() <= 1 and (diff == 0).mean() > 0.99
+    yf = ops.silu_mul(dev(gold["silu_g"]), dev(gold["silu_u"]))
+    np.testing.assert_allclose(to_np(yf), gold["silu_f32"], rtol=1e-5, atol=1e-30)
+    a = torch.from_numpy(gold["add_bf16_a"].view(np.int16)).cuda().view(torch.bfloat16)
+    b = torch.from_numpy(gold["add_bf16_b"].view(np.int16)).cuda().view(torch.bfloat16)
+    c = ops.add(a, b)
+    np.testing.assert_array_equal(c.view(torch.int16).cpu().numpy().view(np.uint16), gold["add_bf16_out"])
+
+
+def test_argmax_ties_and_gap(ops):
+    x = torch.zeros(3, 128256, dtype=torch.bfloat16, device="cuda")
+    x[0, 7] = 3.0
+    x[0, 70000] = 3.0  # tie -> lowest index
+    x[1, 128255] = 1.0
+    x[2, 5] = 2.0
+    x[2, 6] = 1.5
+    idx, gap = ops.argmax(x, with_gap=True)
+    assert idx.tolist() == [7, 128255, 5]
+    assert gap[0].item() == 0.0 and abs(gap[2].item() - 0.5) < 1e-6
+    r = torch.randn(4, 50000, device="cuda")
+    assert torch.equal(ops.argmax(r), torch.argmax(r, dim=1))
+
+
+def test_embedding_matches_reference(ops, gold):
+    t, ids = gold["emb_table"], gold["emb_ids"]
+    out = ops.embedding(dev(ids), dev(t))
+    np.testing.assert_array_equal(to_np(out), gold["emb_out"])
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    bad = ops.embedding(dev(np.array([1, 64], np.int64)), dev(t), status=st)
+    assert int(st.item()) == int(gold["emb_bad_status"][0])
+    assert not bad[1].any()
+    ids32 = dev(ids.astype(np.int32))
+    np.testing.assert_array_equal(to_np(ops.embedding(ids32, dev(t))), gold["emb_out"])
+
+
+def test_embedding_int8_rows(ops, orc):
+    q, s = orc.synth_w8(4, 1, 64, 128, orc.W8_BASE)
+    ids = np.array([3, 0, 63], np.int64)
+    out = ops.embedding(dev(ids), dev(q), row_scales=dev(s))
+    ref = orc.bf16_round(q[ids].astype(np.float32) * s[ids][:, None])
+    np.testing.assert_array_equal(to_np(out), ref)

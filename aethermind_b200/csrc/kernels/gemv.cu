@@ -167,6 +167,15 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_tc_kernel(GemvParams p) {
     }
     __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
     const int m0 = 2 * t, m1 = 2 * t + 1;
+    if constexpr (FMT == AMCU_WFMT_INT8) {
+        // per-output-channel scale (device row order): rows rb*16+g and rb*16+g+8
+        const float s_lo = static_cast<const float*>(p.scales)[rb * 16 + g];
+        const float s_hi = static_cast<const float*>(p.scales)[rb * 16 + g + 8];
+        acc[0] *= s_lo;
+        acc[1] *= s_lo;
+        acc[2] *= s_hi;
+        acc[3] *= s_hi;
+    }
     if constexpr (EPI == AMCU_EPI_SILU_MUL) {
         // c0/c1: gate row, c2/c3: up row of output column 8*rb + g.
         const int64_t col = rb * 8 + g;
@@ -180,12 +189,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_tc_kernel(GemvParams p) {
         }
     } else {
         const int64_t n_lo = rb * 16 + g, n_hi = n_lo + 8;
-        float s_lo = 1.f, s_hi = 1.f;
-        if constexpr (FMT == AMCU_WFMT_INT8) {
-            s_lo = static_cast<const float*>(p.scales)[n_lo];
-            s_hi = static_cast<const float*>(p.scales)[n_hi];
-        }
-        const float v[4] = {acc[0] * s_lo, acc[1] * s_lo, acc[2] * s_hi, acc[3] * s_hi};
+        const float v[4] = {acc[0], acc[1], acc[2], acc[3]};
         const int ms[4] = {m0, m1, m0, m1};
         const int64_t ns[4] = {n_lo, n_lo, n_hi, n_hi};
         const __nv_bfloat16* res = static_cast<const __nv_bfloat16*>(p.residual);

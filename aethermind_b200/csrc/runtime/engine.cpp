@@ -159,8 +159,12 @@ Status KVCacheManager::Init(CudaAllocator& alloc, size_t L, size_t H, size_t T, 
     if (!vb.ok()) return vb.status();
     k_ = std::move(kb.value());
     v_ = std::move(vb.value());
+    // Zero both planes and wait: the engine runs on its own non-blocking stream,
+    // which does not order against the legacy stream a plain cudaMemset uses.
     cudaMemset(k_.data(), 0, plane);
     cudaMemset(v_.data(), 0, plane);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return Status::Internal(std::string("KV cache init: ") + cudaGetErrorString(e));
     total_bytes_ = 2 * plane;
     initialized_ = true;
     return Status::Ok();

@@ -269,8 +269,9 @@ class OracleModel:
         return out[:n], gaps[:n]
 
 
-W4_BASE = 0.02 / 4.6098
-W8_BASE = 0.02 / 73.61
+# same float32 arithmetic as the engine's constants (0.02f / 4.6098f, 0.02f / 73.61f)
+W4_BASE = float(np.float32(0.02) / np.float32(4.6098))
+W8_BASE = float(np.float32(0.02) / np.float32(73.61))
 EMBED_AMP = 0.0692820
 
 

@@ -3,8 +3,8 @@
 Greedy token ids must match the oracle except at documented near-ties: the
 comparison walks the sequence and, at the first mismatch, requires the
 oracle's top-1/top-2 logit gap there to be below the near-tie threshold
-(1e-4 for fp32 models, 0.05 for bf16 models, whose logits carry bf16
-rounding). After a legitimate near-tie flip the sequences diverge, so the
+(1e-4 for fp32 models; 0.125, about 4 bf16 ulps of a logit near 4, for
+bf16 models, whose logits are stored in bf16 as the reference Linear does). After a legitimate near-tie flip the sequences diverge, so the
 remainder is not compared.
 """
 import numpy as np
@@ -67,7 +67,7 @@ def test_quantized_model_matches_oracle(sess_mod, rt, oracle_lib, cfg_name):
     got = s.generate(prompt, 8)
     om = oracle_lib.synthetic_oracle_model(cfg, seed=0)
     ref, gaps = om.generate(prompt.astype(np.int64), 8)
-    n = _compare(got.tolist(), ref.tolist(), gaps, 0.05)
+    n = _compare(got.tolist(), ref.tolist(), gaps, 0.125)
     assert n >= 4
     # batch of 2 equals two single runs (per-row math is independent of the batch)
     p2 = np.stack([prompt, np.random.default_rng(6).integers(0, cfg.vocab, 16).astype(np.uint32)])

@@ -97,6 +97,7 @@ P = C.c_void_p
 _SIGS = {
     "amcu_last_error": (C.c_char_p, []),
     "amcu_version": (C.c_char_p, []),
+    "amcu_device_error": (C.c_int, [C.POINTER(C.c_int32), C.c_int32]),
     "am_error_create": (P, [C.c_int, C.c_char_p]),
     "am_error_destroy": (None, [P]),
     "am_error_code": (C.c_int, [P]),

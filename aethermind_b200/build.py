@@ -59,6 +59,7 @@ def _flags() -> list[str]:
         "-ccbin", _host_cxx(),
         f"-I{INCLUDE}", f"-I{CSRC}",
         "-DAMCU_BUILD",
+        *os.environ.get("AMCU_EXTRA_NVCC_FLAGS", "").split(),
     ]
 
 

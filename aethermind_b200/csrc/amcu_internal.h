@@ -29,6 +29,9 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 int num_sms();
+// Per-device int32 error word that kernels with bounded waits write on timeout
+// (allocated on first use on the current device; nullptr if that fails).
+int32_t* device_error_word();
 
 }  // namespace amcu
 

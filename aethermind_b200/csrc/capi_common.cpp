@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "amcu_internal.h"
@@ -33,6 +34,25 @@ int num_sms() {
     return n;
 }
 
+int32_t* device_error_word() {
+    static int32_t* words[64] = {};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!words[dev]) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, 256) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        cudaMemset(p, 0, 256);
+        cudaDeviceSynchronize();
+        words[dev] = static_cast<int32_t*>(p);
+    }
+    return words[dev];
+}
+
 }  // namespace amcu
 
 namespace {
@@ -47,6 +67,20 @@ struct ErrorObject {
 extern "C" {
 
 const char* amcu_last_error(void) { return amcu::g_last_error.c_str(); }
+
+am_status_code amcu_device_error(int32_t* code, int32_t clear) {
+    int32_t* w = amcu::device_error_word();
+    if (!w) return amcu::set_error(AM_STATUS_INTERNAL, "device error word unavailable");
+    int32_t v = 0;
+    if (cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return amcu::set_error(AM_STATUS_INTERNAL, "reading the device error word failed");
+    if (clear && v != 0) {
+        cudaMemset(w, 0, 4);
+        cudaDeviceSynchronize();
+    }
+    if (code) *code = v;
+    return AM_STATUS_OK;
+}
 
 const char* amcu_version(void) { return "aethermind_b200 0.1 (sm_100a)"; }
 

@@ -70,101 +70,9 @@ __device__ __forceinline__ void unpack_w8_word(uint32_t w, uint32_t& lo, uint32_
 template <typename T>
 __device__ __forceinline__ T epi_store(float v) { return Act<T>::store(v); }
 
-// One CTA = one 16-row tile of W; its warps split K. m <= 8 activation rows.
 template <int FMT, int EPI>
-__global__ void __launch_bounds__(kGemvThreads) gemv_tc_kernel(GemvParams p) {
-    constexpr int W = kGemvThreads / 32;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int64_t rb = blockIdx.x;
-    const int64_t C = p.k / 64;
-    const int64_t per = (C + W - 1) / W;
-    const int64_t c0 = warp * per;
-    const int64_t c1 = c0 + per < C ? c0 + per : C;
-    const bool has_x = g < p.m;
-    const __nv_bfloat16* xrow = static_cast<const __nv_bfloat16*>(p.x) + (has_x ? g : 0) * p.x_stride;
-
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    constexpr int kTileBytes = FMT == AMCU_WFMT_INT4 ? 512 : 1024;
-    const uint8_t* wbase = static_cast<const uint8_t*>(p.w) + (rb * C) * kTileBytes;
-    const int64_t G = p.k / 128;
-
-    constexpr int U = 4;
-    for (int64_t cb = c0; cb < c1; cb += U) {
-        uint4 wv[U][FMT == AMCU_WFMT_INT4 ? 1 : 2];
-        uint4 xv[U][2];
-        uint32_t sv[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int64_t c = cb + u;
-            if (c < c1) {
-                const uint8_t* tp = wbase + c * kTileBytes;
-                if constexpr (FMT == AMCU_WFMT_INT4) {
-                    wv[u][0] = ld_stream_u4(tp + lane * 16);
-                    sv[u] = *reinterpret_cast<const uint32_t*>(static_cast<const __half*>(p.scales) +
-                                                               ((rb * G + (c >> 1)) * 16 + 2 * g));
-                } else {
-                    wv[u][0] = ld_stream_u4(tp + lane * 32);
-                    wv[u][1] = ld_stream_u4(tp + lane * 32 + 16);
-                }
-                if (has_x) {
-                    const __nv_bfloat16* xp = xrow + c * 64 + 16 * t;
-                    xv[u][0] = ld_u4(xp);
-                    xv[u][1] = ld_u4(xp + 8);
-                } else {
-                    xv[u][0] = make_uint4(0, 0, 0, 0);
-                    xv[u][1] = make_uint4(0, 0, 0, 0);
-                }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (cb + u < c1) {
-                const uint32_t X[8] = {xv[u][0].x, xv[u][0].y, xv[u][0].z, xv[u][0].w,
-                                       xv[u][1].x, xv[u][1].y, xv[u][1].z, xv[u][1].w};
-                if constexpr (FMT == AMCU_WFMT_INT4) {
-                    float part[4] = {0.f, 0.f, 0.f, 0.f};
-                    const uint32_t words[4] = {wv[u][0].x, wv[u][0].y, wv[u][0].z, wv[u][0].w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t a[4];
-                        unpack_w4_word(words[j], a);
-                        mma_bf16_16816(part, a, X[2 * j], X[2 * j + 1]);
-                    }
-                    const __half2 s2 = *reinterpret_cast<const __half2*>(&sv[u]);
-                    const float s_lo = __low2float(s2), s_hi = __high2float(s2);
-                    acc[0] = fmaf(part[0], s_lo, acc[0]);
-                    acc[1] = fmaf(part[1], s_lo, acc[1]);
-                    acc[2] = fmaf(part[2], s_hi, acc[2]);
-                    acc[3] = fmaf(part[3], s_hi, acc[3]);
-                } else {
-                    const uint32_t rg[4] = {wv[u][0].x, wv[u][0].y, wv[u][0].z, wv[u][0].w};
-                    const uint32_t rh[4] = {wv[u][1].x, wv[u][1].y, wv[u][1].z, wv[u][1].w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t a[4];
-                        unpack_w8_word(rg[j], a[0], a[2]);
-                        unpack_w8_word(rh[j], a[1], a[3]);
-                        mma_bf16_16816(acc, a, X[2 * j], X[2 * j + 1]);
-                    }
-                }
-            }
-        }
-    }
-
-    // Cross-warp reduction of the 16 x 8 accumulator tile.
-    __shared__ float red[W][32][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) red[warp][lane][i] = acc[i];
-    __syncthreads();
-    if (warp != 0) return;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float s = 0.f;
-#pragma unroll
-        for (int w = 0; w < W; ++w) s += red[w][lane][i];
-        acc[i] = s;
-    }
+__device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int64_t rb, int g, int t, float4 s4) {
+    float acc[4] = {s4.x, s4.y, s4.z, s4.w};
     __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
     const int m0 = 2 * t, m1 = 2 * t + 1;
     if constexpr (FMT == AMCU_WFMT_INT8) {
@@ -205,6 +113,233 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_tc_kernel(GemvParams p) {
     }
 }
 
+// Streaming GEMV. A CTA of 8 warps owns `rb_per_cta` consecutive row blocks
+// (16 output rows each); its warps split K: warp w takes a contiguous run of
+// Tw tiles (16 x 64) of every row block. Each warp walks its (row block, tile)
+// sequence with a register ring of kDepth tiles in flight (one coalesced
+// 16-byte streaming load per lane per INT4 tile, 32 bytes for INT8), so about
+// 128 KB of weights are outstanding per SM at four CTAs per SM. The
+// activations (m <= 8 rows, bf16) are staged once per CTA in shared memory.
+//
+// INT4 tiles are fed to the MMA as the exact bf16 integers 136 + q (one LOP3
+// per register from the packed nibbles); the offset is removed after the MMA
+// by subtracting 136 * sum(x) over the tile's 64 columns, sums computed once
+// per CTA into shared memory. Products (136 + q) * x are exact in fp32, so the
+// correction costs only fp32 rounding.
+//
+// At the end of a row block the warps' 16 x 8 partial tiles meet in shared
+// memory (double-buffered, one barrier) and one warp applies the epilogue.
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kXPad = 16;  // bytes of padding per staged activation row
+#ifndef GEMV_MINB
+#define GEMV_MINB 4
+#endif
+#ifndef GEMV_D4
+#define GEMV_D4 4
+#endif
+
+template <int FMT>
+constexpr int gemv_depth() { return FMT == AMCU_WFMT_INT4 ? GEMV_D4 : 4; }
+
+// (q + 136) in bf16: (w >> 4i) & 0x000F000F selects two nibbles, XOR with
+// 0x43084308 gives bf16 bits of 128 + (n ^ 8) = 136 + q (exact).
+__device__ __forceinline__ void unpack_w4_word_biased(uint32_t w, uint32_t (&a)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(a[i]) : "r"(w >> (4 * i)), "r"(0x000F000Fu), "r"(0x43084308u));
+}
+
+template <int FMT, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvParams p) {
+    constexpr int TB = FMT == AMCU_WFMT_INT4 ? 512 : 1024;
+    constexpr int NV = FMT == AMCU_WFMT_INT4 ? 1 : 2;  // uint4 per lane per tile
+    constexpr int D = gemv_depth<FMT>();               // even
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int C = (int)(p.k / 64), G = (int)(p.k / 128);
+    const int M = (int)p.m;
+    const int xrow = (int)(p.k * 2 + kXPad);
+    float4* red = reinterpret_cast<float4*>(smem);                           // [2][warps][32]
+    float* sx = reinterpret_cast<float*>(smem + 2 * kGemvWarps * 32 * 16);  // [G][8] (INT4)
+    uint8_t* xs = smem + 2 * kGemvWarps * 32 * 16 + (FMT == AMCU_WFMT_INT4 ? G * 8 * 4 : 0);
+
+    const int nrb = (int)(p.n / 16);
+    const int rb0 = blockIdx.x * p.rb_per_cta;
+    const int nr = (rb0 + p.rb_per_cta < nrb ? rb0 + p.rb_per_cta : nrb) - rb0;
+    // K split into runs of `per` tiles; `per` even so a 128-column scale group
+    // never straddles two warps. Runs are padded to a multiple of D so a tile's
+    // ring slot is a compile-time index (padding tiles load nothing).
+    int per = (C + kGemvWarps - 1) / kGemvWarps;
+    per = (per + 1) & ~1;
+    const int c0 = warp * per;
+    const int Tw = c0 >= C ? 0 : (per < C - c0 ? per : C - c0);
+    const int Tp = (Tw + D - 1) / D * D;
+
+    const size_t wstride = (size_t)C * TB;  // bytes between row blocks
+    const size_t sstride = (size_t)G * 32;
+    const uint8_t* wlane = static_cast<const uint8_t*>(p.w) + ((size_t)rb0 * C + c0) * TB + lane * 16 * NV;
+    const uint8_t* slane = static_cast<const uint8_t*>(p.scales) + (((size_t)rb0 * G + c0 / 2) * 16 + 2 * g) * 2;
+
+    uint4 wbuf[D][NV];
+    uint32_t sbuf[D / 2];
+    // weights of tile `tile` of a row block's run into ring slot u; the group
+    // scale of the (even) tile `tile` into scale slot u / 2
+    auto issue_w = [&](int u, const uint8_t* wl, int tile) {
+        if (tile < Tw) {
+#pragma unroll
+            for (int v = 0; v < NV; ++v) wbuf[u][v] = ld_stream_u4(wl + tile * TB + 16 * v);
+        }
+    };
+    auto issue_s = [&](int u, const uint8_t* sl, int tile) {
+        if constexpr (FMT == AMCU_WFMT_INT4)
+            if (tile < Tw) sbuf[u / 2] = __ldg(reinterpret_cast<const unsigned int*>(sl + (tile / 2) * 32));
+    };
+    if (nr > 0) {
+#pragma unroll
+        for (int u = 0; u < D; ++u) {
+            issue_w(u, wlane, u);
+            if ((u & 1) == 0) issue_s(u, slane, u);
+        }
+    }
+
+    // ---- stage activations [m][K] (+16 B per row) and, for INT4, per-group sums of x
+    {
+        const int chunks = (int)(p.k / 8);
+        const __nv_bfloat16* xg = static_cast<const __nv_bfloat16*>(p.x);
+        for (int i = threadIdx.x; i < M * chunks; i += kGemvThreads) {
+            const int m = i / chunks, c = i - m * chunks;
+            *reinterpret_cast<uint4*>(xs + m * xrow + c * 16) = ld_u4(xg + m * p.x_stride + c * 8);
+        }
+    }
+    __syncthreads();
+    if constexpr (FMT == AMCU_WFMT_INT4) {
+        const int segs = G * 8 * M;  // 16-column segments, 8 per group
+        for (int s0 = 0; s0 < segs; s0 += kGemvThreads) {
+            const int s = s0 + threadIdx.x;
+            float sum = 0.f;
+            int m = 0, grp = 0;
+            if (s < segs) {
+                m = s / (G * 8);
+                const int r = s - m * G * 8;
+                grp = r >> 3;
+                const uint8_t* xp = xs + m * xrow + (grp * 128 + (r & 7) * 16) * 2;
+                const uint4 a = *reinterpret_cast<const uint4*>(xp), b = *reinterpret_cast<const uint4*>(xp + 16);
+                const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) sum += __uint_as_float(w[j] << 16) + __uint_as_float(w[j] & 0xffff0000u);
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            if (s < segs && (s & 7) == 0) sx[grp * 8 + m] = sum;
+        }
+        for (int i = threadIdx.x; i < G * 8; i += kGemvThreads)
+            if ((i & 7) >= M) sx[i] = 0.f;  // rows without activations add nothing
+        __syncthreads();
+    }
+
+    // Lanes whose activation row does not exist (g >= M) read row 0: they only
+    // feed MMA output columns g >= M, which the epilogue never stores.
+    const uint8_t* xw = xs + (g < M ? g : 0) * xrow + (c0 * 64 + 16 * t) * 2;  // + 128 B per tile
+    const float* sxw = sx + (c0 / 2) * 8 + 2 * t;                              // + 8 floats per group
+    int par = 0;
+    for (int r = 0; r < nr; ++r, par ^= 1) {
+        const uint8_t* wl = wlane + r * wstride;
+        const uint8_t* sl = slane + r * sstride;
+        const uint8_t* xp = xw;
+        const float* sxp = sxw;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int j = 0; j < Tp; j += D, xp += D * 128, sxp += (D / 2) * 8) {
+            // where this group's slots get refilled: the next group of this row
+            // block, or the first group of the next one (uniform per group)
+            const bool same = j + D < Tp;
+            const bool more = same || r + 1 < nr;
+            const int ntile = same ? j + D : 0;
+            const uint8_t* nwp = (same ? wl : wl + wstride) + ntile * TB;
+            const uint8_t* nsp = (same ? sl : sl + sstride) + (ntile / 2) * 32;
+            const int nlim = Tw - ntile;  // slots u < nlim get a real tile
+#pragma unroll
+            for (int u = 0; u < D; u += 2) {
+                if (j + u < Tw) {  // Tw is even: both tiles of the pair are real
+                    float part[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const uint4 x0 = *reinterpret_cast<const uint4*>(xp + (u + h) * 128);
+                        const uint4 x1 = *reinterpret_cast<const uint4*>(xp + (u + h) * 128 + 16);
+                        const uint32_t X[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                        if constexpr (FMT == AMCU_WFMT_INT4) {
+                            const uint32_t words[4] = {wbuf[u + h][0].x, wbuf[u + h][0].y, wbuf[u + h][0].z,
+                                                       wbuf[u + h][0].w};
+#pragma unroll
+                            for (int jj = 0; jj < 4; ++jj) {
+                                uint32_t a[4];
+                                unpack_w4_word_biased(words[jj], a);
+                                mma_bf16_16816(part, a, X[2 * jj], X[2 * jj + 1]);
+                            }
+                        } else {
+                            const uint32_t rg[4] = {wbuf[u + h][0].x, wbuf[u + h][0].y, wbuf[u + h][0].z,
+                                                    wbuf[u + h][0].w};
+                            const uint32_t rh[4] = {wbuf[u + h][1].x, wbuf[u + h][1].y, wbuf[u + h][1].z,
+                                                    wbuf[u + h][1].w};
+#pragma unroll
+                            for (int jj = 0; jj < 4; ++jj) {
+                                uint32_t a[4];
+                                unpack_w8_word(rg[jj], a[0], a[2]);
+                                unpack_w8_word(rh[jj], a[1], a[3]);
+                                mma_bf16_16816(acc, a, X[2 * jj], X[2 * jj + 1]);
+                            }
+                        }
+                        if (more && u + h < nlim) {
+#pragma unroll
+                            for (int v = 0; v < NV; ++v)
+                                wbuf[u + h][v] = ld_stream_u4(nwp + (u + h) * TB + 16 * v);
+                        }
+                    }
+                    if constexpr (FMT == AMCU_WFMT_INT4) {
+                        // part holds sum (136 + q) x over the group's 128 columns
+                        const float2 s2x = *reinterpret_cast<const float2*>(sxp + (u / 2) * 8);
+                        const __half2 s2 = *reinterpret_cast<const __half2*>(&sbuf[u / 2]);
+                        const float s_lo = __low2float(s2), s_hi = __high2float(s2);
+                        acc[0] = fmaf(fmaf(-136.f, s2x.x, part[0]), s_lo, acc[0]);
+                        acc[1] = fmaf(fmaf(-136.f, s2x.y, part[1]), s_lo, acc[1]);
+                        acc[2] = fmaf(fmaf(-136.f, s2x.x, part[2]), s_hi, acc[2]);
+                        acc[3] = fmaf(fmaf(-136.f, s2x.y, part[3]), s_hi, acc[3]);
+                        if (more && u < nlim)
+                            sbuf[u / 2] = __ldg(reinterpret_cast<const unsigned int*>(nsp + (u / 2) * 32));
+                    }
+                } else if (more && u < nlim) {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int v = 0; v < NV; ++v) wbuf[u + h][v] = ld_stream_u4(nwp + (u + h) * TB + 16 * v);
+                    if constexpr (FMT == AMCU_WFMT_INT4)
+                        sbuf[u / 2] = __ldg(reinterpret_cast<const unsigned int*>(nsp + (u / 2) * 32));
+                }
+            }
+        }
+        // row-block end: publish this warp's partial tile, meet the other
+        // warps, and let one warp reduce and apply the epilogue
+        red[(par * kGemvWarps + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        named_bar_sync(1, kGemvThreads);
+        const int rb = rb0 + r;
+        if (warp == rb % kGemvWarps) {
+            float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < kGemvWarps; ++w) {
+                const float4 v = red[(par * kGemvWarps + w) * 32 + lane];
+                s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
+            }
+            gemv_epilogue<FMT, EPI>(p, rb, g, t, s4);
+        }
+    }
+}
+
+template <int FMT>
+static size_t gemv_smem_bytes(int64_t m, int64_t k) {
+    return 2 * kGemvWarps * 32 * 16 + (FMT == AMCU_WFMT_INT4 ? (k / 128) * 8 * 4 : 0) + m * (k * 2 + kXPad);
+}
+
 // Plain fp32 weights (the fp32 tiny model): one thread per output, fp32 FMA.
 template <typename T, int EPI>
 __global__ void gemm_plain_kernel(GemvParams p) {
@@ -233,13 +368,39 @@ __global__ void gemm_plain_kernel(GemvParams p) {
     }
 }
 
+template <int FMT, int EPI>
+static void launch_gemv_one(GemvParams p, cudaStream_t s) {
+    constexpr int kMaxSmem = 200 * 1024;
+    static int max_ctas = 0;  // per instantiation (one device per process on this path)
+    if (max_ctas == 0) {
+        cudaFuncSetAttribute(gemv_tc_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+        int per_sm = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tc_kernel<FMT, EPI>, kGemvThreads, 16 * 1024);
+        max_ctas = (per_sm > 0 ? per_sm : 1) * num_sms();
+    }
+    const int64_t nrb = p.n / 16;
+    p.rb_per_cta = (int)((nrb + max_ctas - 1) / max_ctas);
+    const int64_t grid = (nrb + p.rb_per_cta - 1) / p.rb_per_cta;
+    // The activation rows are staged in shared memory; when m rows of this K do
+    // not fit, the rows go in slices (each slice streams W again).
+    int64_t fit = p.m;
+    while (fit > 1 && gemv_smem_bytes<FMT>(fit, p.k) > (size_t)kMaxSmem) --fit;
+    for (int64_t m0 = 0; m0 < p.m; m0 += fit) {
+        GemvParams q = p;
+        q.m = p.m - m0 < fit ? p.m - m0 : fit;
+        q.x = static_cast<const __nv_bfloat16*>(p.x) + m0 * p.x_stride;
+        q.y = static_cast<__nv_bfloat16*>(p.y) + m0 * p.y_stride;
+        if (p.residual) q.residual = static_cast<const __nv_bfloat16*>(p.residual) + m0 * p.y_stride;
+        gemv_tc_kernel<FMT, EPI><<<(unsigned)grid, kGemvThreads, gemv_smem_bytes<FMT>(q.m, q.k), s>>>(q);
+    }
+}
+
 template <int FMT>
 static void launch_gemv_fmt(const GemvParams& p, int epi, cudaStream_t s) {
-    const dim3 grid((unsigned)(p.n / 16));
     switch (epi) {
-        case AMCU_EPI_STORE: gemv_tc_kernel<FMT, AMCU_EPI_STORE><<<grid, kGemvThreads, 0, s>>>(p); break;
-        case AMCU_EPI_RESIDUAL_ADD: gemv_tc_kernel<FMT, AMCU_EPI_RESIDUAL_ADD><<<grid, kGemvThreads, 0, s>>>(p); break;
-        default: gemv_tc_kernel<FMT, AMCU_EPI_SILU_MUL><<<grid, kGemvThreads, 0, s>>>(p); break;
+        case AMCU_EPI_STORE: launch_gemv_one<FMT, AMCU_EPI_STORE>(p, s); break;
+        case AMCU_EPI_RESIDUAL_ADD: launch_gemv_one<FMT, AMCU_EPI_RESIDUAL_ADD>(p, s); break;
+        default: launch_gemv_one<FMT, AMCU_EPI_SILU_MUL>(p, s); break;
     }
 }
 

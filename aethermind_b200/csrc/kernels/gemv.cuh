@@ -16,6 +16,8 @@ struct GemvParams {
     const void* residual;
     int64_t m, n, k;
     int64_t x_stride, y_stride;
+    int32_t* err;     // device error word for bounded waits
+    int rb_per_cta;   // set by the launcher
 };
 
 // Quantized (INT4 / INT8 tile16x64) GEMV, m <= kGemvMaxM, bf16 activations.

@@ -47,6 +47,7 @@ GemvParams make_params(const AmcuLinearArgs* a) {
     p.k = a->w.k;
     p.x_stride = a->x_stride ? a->x_stride : a->w.k;
     p.y_stride = a->y_stride ? a->y_stride : (a->epilogue == AMCU_EPI_SILU_MUL ? a->w.n / 2 : a->w.n);
+    p.err = device_error_word();
     return p;
 }
 

@@ -156,7 +156,7 @@ Status SliceCanon(am_model_s* m, const Canon& src, int64_t r0, int64_t nr, int64
         AM_CUDA(cudaMemcpy2DAsync(dst.s.data(), sdp, src.s.as<char>() + r0 * ssp + soff, ssp, sdp, nr,
                                   cudaMemcpyDeviceToDevice, s));
     }
-    return Status::Ok();
+    return CudaOk(cudaStreamSynchronize(s), "shard copy");  // src may be freed next
 }
 
 // Prepacks a canonical matrix into rows [row0, row0 + n) of a device weight.
@@ -166,7 +166,10 @@ Status PackInto(am_model_s* m, LinearWeight& lw, int64_t row0, const Canon& cn) 
     char* sd = lw.s.data() ? static_cast<char*>(lw.s.data()) + row0 * ScaleRowBytes(c, lw.w.k) : nullptr;
     am_status_code st = amcu_prepack_weight(c.weight_format, c.act_dtype, cn.n, cn.k, c.group_size, cn.q.data(),
                                             cn.s.data(), qd, sd, m->rt->stream);
-    return Status::FromAm(st, amcu_last_error());
+    AM_RETURN_IF_ERROR(Status::FromAm(st, amcu_last_error()));
+    // The canonical staging buffers are freed by the caller right after this;
+    // the copy on the engine's non-blocking stream must have read them first.
+    return CudaOk(cudaStreamSynchronize(m->rt->stream), "prepack");
 }
 
 enum class Split { kNone, kRows, kCols };
@@ -540,7 +543,9 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
     AM_RETURN_IF_ERROR(EnsureWorkspace(s, s->decode));
 
     // stage the prompt (pinned host -> device)
-    const size_t need = B * P * 8 + c.max_batch * N * 12;
+    // pinned staging: prompt [B*P] int64 | tokens [max_batch*out_cap] int64 |
+    // gaps [max_batch*out_cap] float | status int32
+    const size_t need = B * P * 8 + c.max_batch * s->out_cap * 12 + 16;
     if (s->pinned_bytes < need) {
         if (s->pinned) cudaFreeHost(s->pinned);
         AM_CUDA(cudaMallocHost(&s->pinned, need));
@@ -557,6 +562,10 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
     AM_RETURN_IF_ERROR(s->exec.Execute(s->prefill, stream, &s->ws, &kv));
     AM_RETURN_IF_ERROR(RunAdvance(s, B, (int32_t)P, st));
     AM_CUDA(cudaEventRecord(s->ev[1], st));
+    // Finish the eagerly launched prefill before the decode loop starts: the
+    // decode graph (captured below on first use) reads the positions and the
+    // token counter the prefill's last kernel wrote.
+    AM_CUDA(cudaStreamSynchronize(st));
 
     const bool use_graph = s->cfg.use_cuda_graph != 0;
     if (use_graph && N > 1 && s->graph_B != B) {
@@ -584,13 +593,14 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
     }
     AM_CUDA(cudaEventRecord(s->ev[2], st));
     int64_t* ho = hp + B * P;
-    float* hg = reinterpret_cast<float*>(ho + c.max_batch * N);
+    float* hg = reinterpret_cast<float*>(ho + c.max_batch * s->out_cap);
     AM_CUDA(cudaMemcpyAsync(ho, s->out_tokens.data(), B * s->out_cap * 8, cudaMemcpyDeviceToHost, st));
     AM_CUDA(cudaMemcpyAsync(hg, s->gaps.data(), B * s->out_cap * 4, cudaMemcpyDeviceToHost, st));
     int32_t status_h = 0;
-    AM_CUDA(cudaMemcpyAsync(hg + B * s->out_cap, s->status.data(), 4, cudaMemcpyDeviceToHost, st));
+    int32_t* hstatus = reinterpret_cast<int32_t*>(hg + c.max_batch * s->out_cap);
+    AM_CUDA(cudaMemcpyAsync(hstatus, s->status.data(), 4, cudaMemcpyDeviceToHost, st));
     AM_CUDA(cudaStreamSynchronize(st));
-    std::memcpy(&status_h, hg + B * s->out_cap, 4);
+    status_h = *hstatus;
     if (status_h != 0) return Status(static_cast<StatusCode>(status_h), "device reported an out-of-range index");
     AM_RETURN_IF_ERROR(kv.CommitUntil(P + N - 1));
     out.resize(B * N);

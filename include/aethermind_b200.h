@@ -69,6 +69,10 @@ const char* am_error_message(am_error_handle error);
 const char* amcu_last_error(void);
 /* Library version string and the CUDA arch it was built for ("sm_100a"). */
 const char* amcu_version(void);
+/* Device error word of the current device: non-zero when a kernel's bounded
+ * wait ran out (the kernel recorded a code and returned instead of hanging).
+ * clear != 0 resets it. Synchronizes with the device. */
+am_status_code amcu_device_error(int32_t* code, int32_t clear);
 
 /* Element types (subset of the reference DataType used on the path). */
 typedef enum amcu_dtype {

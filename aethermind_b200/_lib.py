@@ -49,7 +49,7 @@ class AmcuLinearArgs(C.Structure):
     _fields_ = [("x", C.c_void_p), ("w", AmcuWeight), ("y", C.c_void_p), ("residual", C.c_void_p),
                 ("m", C.c_int64), ("x_stride", C.c_int64), ("y_stride", C.c_int64),
                 ("act_dtype", C.c_int32), ("epilogue", C.c_int32), ("workspace", C.c_void_p),
-                ("workspace_size", C.c_size_t)]
+                ("workspace_size", C.c_size_t), ("norm_weight", C.c_void_p), ("norm_eps", C.c_float)]
 
 
 class AmcuRopeKvArgs(C.Structure):
@@ -58,7 +58,7 @@ class AmcuRopeKvArgs(C.Structure):
                 ("v_cache", C.c_void_p), ("slot_stride", C.c_int64), ("capacity", C.c_int64),
                 ("seq_pos", C.c_void_p), ("rows", C.c_int64), ("rows_per_seq", C.c_int64),
                 ("n_q_heads", C.c_int64), ("n_kv_heads", C.c_int64), ("head_dim", C.c_int64),
-                ("theta", C.c_double), ("dtype", C.c_int32), ("status", C.c_void_p)]
+                ("theta", C.c_double), ("dtype", C.c_int32), ("status", C.c_void_p), ("cos_sin", C.c_void_p)]
 
 
 class AmcuAttentionArgs(C.Structure):
@@ -118,12 +118,15 @@ _SIGS = {
     "amcu_gemm_w8_prefill": (C.c_int, [C.POINTER(AmcuLinearArgs), P]),
     "amcu_gemm_w4g128_prefill": (C.c_int, [C.POINTER(AmcuLinearArgs), P]),
     "amcu_rope_kv_write": (C.c_int, [C.POINTER(AmcuRopeKvArgs), P]),
+    "amcu_rope_table": (C.c_int, [C.c_double, C.c_int64, C.c_int64, P, P]),
     "amcu_attention_workspace_bytes": (C.c_size_t, [C.POINTER(AmcuAttentionArgs)]),
     "amcu_attn_decode": (C.c_int, [C.POINTER(AmcuAttentionArgs), P]),
     "amcu_attn_prefill": (C.c_int, [C.POINTER(AmcuAttentionArgs), P]),
     "amcu_silu_mul": (C.c_int, [P, P, P, C.c_int64, C.c_int32, P]),
     "amcu_add": (C.c_int, [P, P, P, C.c_int64, C.c_int32, P]),
     "amcu_argmax": (C.c_int, [P, C.c_int64, C.c_int64, C.c_int64, C.c_int32, P, P, P]),
+    "amcu_argmax_workspace_bytes": (C.c_size_t, [C.c_int64]),
+    "amcu_argmax_ws": (C.c_int, [P, C.c_int64, C.c_int64, C.c_int64, C.c_int32, P, P, P, C.c_size_t, P]),
     "amcu_embedding": (C.c_int, [C.POINTER(AmcuEmbeddingArgs), P]),
     "am_runtime_create": (P, [C.POINTER(AmConfig)]),
     "am_runtime_destroy": (None, [P]),

@@ -175,29 +175,209 @@ __global__ void __launch_bounds__(kAttnThreads) attn_splitk_kernel(AttnKParams p
     }
 }
 
+
+// Decode kernel (one query row per sequence, long context): the same split /
+// combine structure, with a warp scoring 8 keys at a time. Lane 4k+q holds
+// quarter q of key k's head_dim: four 16-byte K loads per lane, a two-shuffle
+// reduction, one online-softmax update per 8-key block, then P*V with lane l
+// owning head_dim/32 output dims of every head (V rows read coalesced).
+template <typename T, int GRP, int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnKParams p) {
+    constexpr int NW = kAttnThreads / 32;
+    constexpr int DQ = D / 4;   // dims per lane in the QK phase
+    constexpr int DL = D / 32;  // dims per lane in the PV phase
+    static_assert(sizeof(T) == 2, "bf16 only");
+    const int split = blockIdx.x, kvh = blockIdx.y;
+    const int64_t row = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kk = lane >> 2, qd = lane & 3;
+    const int64_t b = row / p.rows_per_seq;
+    const int64_t pos = (int64_t)p.seq_pos[b] + row % p.rows_per_seq;
+    const int64_t L = pos + 1;
+    int64_t chunk = (L + p.nsplit - 1) / p.nsplit;
+    chunk = (chunk + 7) / 8 * 8;
+    const int64_t k_begin = (int64_t)split * chunk;
+    const int64_t k_end = k_begin + chunk < L ? k_begin + chunk : L;
+
+    __shared__ __align__(16) float qs[GRP][D];
+    __shared__ float sm_m[NW][GRP], sm_l[NW][GRP];
+    __shared__ float sm_o[NW][GRP][D];
+    const T* qrow = static_cast<const T*>(p.q) + row * p.q_stride + (int64_t)kvh * GRP * D;
+    for (int i = threadIdx.x; i < GRP * D; i += kAttnThreads) qs[i / D][i % D] = Act<T>::load(qrow[i]) * p.scale_log2;
+    __syncthreads();
+
+    const T* kbase = static_cast<const T*>(p.kc) + b * p.slot_stride + (int64_t)kvh * p.capacity * D;
+    const T* vbase = static_cast<const T*>(p.vc) + b * p.slot_stride + (int64_t)kvh * p.capacity * D;
+
+    float m[GRP], l[GRP], acc[GRP][DL];
+#pragma unroll
+    for (int h = 0; h < GRP; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DL; ++i) acc[h][i] = 0.f;
+    }
+
+    for (int64_t kb = k_begin + warp * 8; kb < k_end; kb += NW * 8) {
+        const int64_t key = kb + kk;
+        const bool valid = key < k_end;
+        // K quarter of this lane's key, V slices of the block's 8 keys
+        uint4 kv4[DQ / 8];
+#pragma unroll
+        for (int i = 0; i < DQ / 8; ++i)
+            kv4[i] = valid ? *reinterpret_cast<const uint4*>(kbase + key * D + qd * DQ + i * 8) : make_uint4(0, 0, 0, 0);
+        const int nk = (int)(k_end - kb < 8 ? k_end - kb : 8);
+        float vf[8][DL];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j < nk) {
+                const T* vr = vbase + (kb + j) * D + lane * DL;
+                if constexpr (DL == 4) {
+                    const uint2 u = *reinterpret_cast<const uint2*>(vr);
+                    vf[j][0] = __uint_as_float(u.x << 16); vf[j][1] = __uint_as_float(u.x & 0xffff0000u);
+                    vf[j][2] = __uint_as_float(u.y << 16); vf[j][3] = __uint_as_float(u.y & 0xffff0000u);
+                } else {
+                    const uint32_t u = *reinterpret_cast<const uint32_t*>(vr);
+                    vf[j][0] = __uint_as_float(u << 16); vf[j][1] = __uint_as_float(u & 0xffff0000u);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < DL; ++i) vf[j][i] = 0.f;
+            }
+        }
+        float s[GRP];
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) s[h] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DQ / 8; ++i) {
+            const uint32_t w4[4] = {kv4[i].x, kv4[i].y, kv4[i].z, kv4[i].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float k0 = __uint_as_float(w4[e] << 16), k1 = __uint_as_float(w4[e] & 0xffff0000u);
+                const int dd = qd * DQ + i * 8 + 2 * e;
+#pragma unroll
+                for (int h = 0; h < GRP; ++h) {
+                    const float2 qq = *reinterpret_cast<const float2*>(&qs[h][dd]);
+                    s[h] = fmaf(qq.x, k0, fmaf(qq.y, k1, s[h]));
+                }
+            }
+        }
+        float pr[GRP];
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) {
+            s[h] += __shfl_xor_sync(0xffffffffu, s[h], 1);
+            s[h] += __shfl_xor_sync(0xffffffffu, s[h], 2);
+            const float sv = valid ? s[h] : -INFINITY;
+            float bm = fmaxf(sv, __shfl_xor_sync(0xffffffffu, sv, 4));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+            const float mn = fmaxf(m[h], bm);
+            const float corr = exp2f(m[h] - mn);
+            pr[h] = valid ? exp2f(sv - mn) : 0.f;
+            float bs = pr[h] + __shfl_xor_sync(0xffffffffu, pr[h], 4);
+            bs += __shfl_xor_sync(0xffffffffu, bs, 8);
+            bs += __shfl_xor_sync(0xffffffffu, bs, 16);
+            l[h] = l[h] * corr + bs;
+            m[h] = mn;
+#pragma unroll
+            for (int i = 0; i < DL; ++i) acc[h][i] *= corr;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+            for (int h = 0; h < GRP; ++h) {
+                const float pj = __shfl_sync(0xffffffffu, pr[h], 4 * j);
+#pragma unroll
+                for (int i = 0; i < DL; ++i) acc[h][i] = fmaf(pj, vf[j][i], acc[h][i]);
+            }
+        }
+    }
+
+    if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) { sm_m[warp][h] = m[h]; sm_l[warp][h] = l[h]; }
+    }
+#pragma unroll
+    for (int h = 0; h < GRP; ++h)
+#pragma unroll
+        for (int i = 0; i < DL; ++i) sm_o[warp][h][lane * DL + i] = acc[h][i];
+    __syncthreads();
+    for (int e = threadIdx.x; e < GRP * D; e += kAttnThreads) {
+        const int h = e / D, dd = e % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w][h]);
+        float Ls = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const float f = exp2f(sm_m[w][h] - M);
+                Ls += sm_l[w][h] * f;
+                O += sm_o[w][h][dd] * f;
+            }
+        }
+        const int64_t qh = (int64_t)kvh * GRP + h;
+        if (p.nsplit == 1) {
+            T* o = static_cast<T*>(p.out) + row * p.out_stride + qh * D;
+            o[dd] = Act<T>::store(O / Ls);
+        } else {
+            float* w = p.ws + ((row * p.nq + qh) * p.nsplit + split) * (D + 2);
+            w[2 + dd] = O;
+            if (dd == 0) { w[0] = M; w[1] = Ls; }
+        }
+    }
+}
+
+// Merges the split partials of one (row, head): every split's (max, sum)
+// is read in parallel, the weights exp2(m_s - M) go through shared memory,
+// then each thread sums its output dim over the splits.
+constexpr int kMaxSplits = 64;
 template <typename T, int D>
-__global__ void attn_combine_kernel(AttnKParams p) {
+__global__ void __launch_bounds__(D) attn_combine_kernel(AttnKParams p) {
     const int64_t row = blockIdx.x / p.nq, qh = blockIdx.x % p.nq;
     const float* w = p.ws + (row * p.nq + qh) * p.nsplit * (D + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, w[s * (D + 2)]);
-    for (int dd = threadIdx.x; dd < D; dd += blockDim.x) {
-        float Ls = 0.f, O = 0.f;
-        for (int s = 0; s < p.nsplit; ++s) {
-            const float* ws = w + s * (D + 2);
-            if (ws[0] == -INFINITY) continue;
-            const float f = exp2f(ws[0] - M);
-            Ls += ws[1] * f;
-            O += ws[2 + dd] * f;
-        }
-        static_cast<T*>(p.out)[row * p.out_stride + qh * D + dd] = Act<T>::store(O / Ls);
+    __shared__ float f[kMaxSplits];
+    __shared__ float red[D / 32];
+    __shared__ float total;
+    const int t = threadIdx.x;
+    const float ms = t < p.nsplit ? w[t * (D + 2)] : -INFINITY;
+    float M = warp_max(ms);
+    if ((t & 31) == 0) red[t >> 5] = M;
+    __syncthreads();
+    M = red[0];
+#pragma unroll
+    for (int i = 1; i < D / 32; ++i) M = fmaxf(M, red[i]);
+    __syncthreads();
+    float fl = 0.f;
+    if (t < p.nsplit) {
+        const float fs = ms == -INFINITY ? 0.f : exp2f(ms - M);
+        f[t] = fs;
+        fl = fs * w[t * (D + 2) + 1];
     }
+    fl = warp_sum(fl);
+    if ((t & 31) == 0) red[t >> 5] = fl;
+    __syncthreads();
+    if (t == 0) {
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) s += red[i];
+        total = s;
+    }
+    __syncthreads();
+    float O = 0.f;
+    for (int s = 0; s < p.nsplit; ++s) O = fmaf(f[s], w[s * (D + 2) + 2 + t], O);
+    static_cast<T*>(p.out)[row * p.out_stride + qh * D + t] = Act<T>::store(O / total);
 }
 
 template <typename T, int GRP, int D>
 static void launch_attn(const AttnKParams& p, int64_t rows, cudaStream_t s) {
     const dim3 grid((unsigned)p.nsplit, (unsigned)p.nkv, (unsigned)rows);
-    attn_splitk_kernel<T, GRP, D><<<grid, kAttnThreads, 0, s>>>(p);
+    if constexpr (sizeof(T) == 2) {
+        if (p.rows_per_seq == 1) attn_decode_kernel<T, GRP, D><<<grid, kAttnThreads, 0, s>>>(p);
+        else attn_splitk_kernel<T, GRP, D><<<grid, kAttnThreads, 0, s>>>(p);
+    } else {
+        attn_splitk_kernel<T, GRP, D><<<grid, kAttnThreads, 0, s>>>(p);
+    }
     if (p.nsplit > 1) attn_combine_kernel<T, D><<<(unsigned)(rows * p.nq), D, 0, s>>>(p);
 }
 
@@ -222,10 +402,10 @@ int choose_splits(const AmcuAttentionArgs* a) {
     if (a->num_splits > 0) return a->num_splits;
     if (a->rows_per_seq > 1) return 1;
     const int64_t ctas = a->n_kv_heads * a->rows;
-    int64_t by_len = (a->max_context + 63) / 64;
-    int64_t by_sm = (2 * num_sms() + ctas - 1) / ctas;
+    int64_t by_len = (a->max_context + 31) / 32;
+    int64_t by_sm = (4 * num_sms() + ctas - 1) / ctas;
     int64_t s = by_len < by_sm ? by_len : by_sm;
-    if (s > 64) s = 64;
+    if (s > kMaxSplits) s = kMaxSplits;
     return (int)(s < 1 ? 1 : s);
 }
 
@@ -239,6 +419,8 @@ am_status_code validate_attn(const AmcuAttentionArgs* a, const char* who) {
     AMCU_REQUIRE(a->head_dim == 64 || a->head_dim == 128, "%s: head_dim must be 64 or 128", who);
     AMCU_REQUIRE(a->dtype == AMCU_F32 || a->dtype == AMCU_BF16, "%s: dtype must be f32 or bf16", who);
     AMCU_REQUIRE(a->rows_per_seq > 0 && a->capacity > 0, "%s: bad rows_per_seq/capacity", who);
+    AMCU_REQUIRE(a->num_splits >= 0 && a->num_splits <= kMaxSplits, "%s: num_splits must be in [0, %d]", who,
+                 kMaxSplits);
     const int64_t elt = a->dtype == AMCU_F32 ? 4 : 2;
     AMCU_REQUIRE(aligned(a->q, 16) && aligned(a->k_cache, 16) && aligned(a->v_cache, 16),
                  "%s: q and caches must be 16-byte aligned", who);

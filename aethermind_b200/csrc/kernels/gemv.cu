@@ -213,6 +213,46 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
         }
     }
     __syncthreads();
+    if (p.norm_w) {
+        // fused RMSNorm of the staged rows: warp w owns row w, as
+        // y = round(x * (mean(x^2) + eps)^-1/2 * w) (the RMSNorm kernel's formula)
+        float* inv_s = reinterpret_cast<float*>(red);  // red is free until the first row-block end
+        if (warp < M) {
+            const uint8_t* xr = xs + warp * xrow;
+            float ss = 0.f;
+            for (int c = lane; c < (int)(p.k / 8); c += 32) {
+                const uint4 v = *reinterpret_cast<const uint4*>(xr + c * 16);
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float a = __uint_as_float(w4[j] << 16), b = __uint_as_float(w4[j] & 0xffff0000u);
+                    ss += a * a + b * b;
+                }
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) inv_s[warp] = 1.0f / sqrtf(ss / (float)p.k + p.eps);
+        }
+        __syncthreads();
+        const int chunks = (int)(p.k / 8);
+        const __nv_bfloat16* nw = static_cast<const __nv_bfloat16*>(p.norm_w);
+        for (int i = threadIdx.x; i < M * chunks; i += kGemvThreads) {
+            const int m = i / chunks, c = i - m * chunks;
+            uint4* xp = reinterpret_cast<uint4*>(xs + m * xrow + c * 16);
+            const uint4 v = *xp, wv = ld_u4(nw + c * 8);
+            const float inv = inv_s[m];
+            const uint32_t a[4] = {v.x, v.y, v.z, v.w}, b[4] = {wv.x, wv.y, wv.z, wv.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float lo = __uint_as_float(a[j] << 16) * inv * __uint_as_float(b[j] << 16);
+                const float hi = __uint_as_float(a[j] & 0xffff0000u) * inv * __uint_as_float(b[j] & 0xffff0000u);
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
+                o[j] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            *xp = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        __syncthreads();
+    }
     if constexpr (FMT == AMCU_WFMT_INT4) {
         const int segs = G * 8 * M;  // 16-column segments, 8 per group
         for (int s0 = 0; s0 < segs; s0 += kGemvThreads) {

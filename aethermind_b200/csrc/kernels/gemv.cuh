@@ -17,6 +17,8 @@ struct GemvParams {
     int64_t m, n, k;
     int64_t x_stride, y_stride;
     int32_t* err;     // device error word for bounded waits
+    const void* norm_w;  // optional fused RMSNorm weight [k] (bf16)
+    float eps;
     int rb_per_cta;   // set by the launcher
 };
 

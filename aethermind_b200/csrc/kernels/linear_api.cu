@@ -16,6 +16,9 @@ am_status_code validate_linear(const AmcuLinearArgs* a, const char* who) {
     AMCU_REQUIRE(a->x && a->y && w.data, "%s: null pointer", who);
     AMCU_REQUIRE(a->epilogue >= AMCU_EPI_STORE && a->epilogue <= AMCU_EPI_SILU_MUL, "%s: bad epilogue", who);
     AMCU_REQUIRE(a->epilogue != AMCU_EPI_RESIDUAL_ADD || a->residual, "%s: residual epilogue needs residual", who);
+    AMCU_REQUIRE(!a->norm_weight || w.format != AMCU_WFMT_PLAIN,
+                 "%s: the fused RMSNorm is available for quantized weights", who);
+    AMCU_REQUIRE(!a->norm_weight || aligned(a->norm_weight, 16), "%s: norm weight must be 16-byte aligned", who);
     AMCU_REQUIRE(a->epilogue != AMCU_EPI_SILU_MUL || w.gate_up_interleaved || w.format == AMCU_WFMT_PLAIN,
                  "%s: SILU_MUL epilogue needs a weight from amcu_prepack_gate_up", who);
     if (w.format == AMCU_WFMT_PLAIN) {
@@ -48,6 +51,8 @@ GemvParams make_params(const AmcuLinearArgs* a) {
     p.x_stride = a->x_stride ? a->x_stride : a->w.k;
     p.y_stride = a->y_stride ? a->y_stride : (a->epilogue == AMCU_EPI_SILU_MUL ? a->w.n / 2 : a->w.n);
     p.err = device_error_word();
+    p.norm_w = a->norm_weight;
+    p.eps = a->norm_eps;
     return p;
 }
 
@@ -77,7 +82,7 @@ am_status_code run_gemm(const AmcuLinearArgs* a, cudaStream_t s) {
     g.m = p.m; g.n = p.n; g.k = p.k; g.x_stride = p.x_stride; g.y_stride = p.y_stride;
     g.workspace = a->workspace;
     g.workspace_size = a->workspace_size;
-    if (gemm_tc_supported(g, a->w.format)) {
+    if (!a->norm_weight && gemm_tc_supported(g, a->w.format)) {
         am_status_code st = launch_gemm_tc(g, a->w.format, a->epilogue, s);
         if (st != AM_STATUS_OK) return st;
         return check_launch("amcu_gemm_tc");

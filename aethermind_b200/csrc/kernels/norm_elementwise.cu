@@ -136,6 +136,73 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ logi
     }
 }
 
+// Two-phase argmax for long rows: `parts` CTAs per row each reduce a slice
+// with 16-byte loads into a Top2 partial; one CTA per row merges them.
+constexpr int kArgmaxParts = 64;
+template <typename T>
+__global__ void __launch_bounds__(256) argmax_partial_kernel(const T* __restrict__ logits, int64_t vocab,
+                                                             int64_t stride, Top2* __restrict__ parts) {
+    const int64_t row = blockIdx.y;
+    const T* l = logits + row * stride;
+    constexpr int V = 16 / sizeof(T);
+    const int64_t nvec = vocab / V;
+    const int64_t per = (nvec + gridDim.x - 1) / gridDim.x;
+    const int64_t v0 = blockIdx.x * per, v1 = v0 + per < nvec ? v0 + per : nvec;
+    Top2 t{-INFINITY, INT64_MAX, -INFINITY};
+    auto consider = [&](float v, int64_t j) {
+        if (better(v, j, t.v1, t.i1)) { t.v2 = t.v1; t.v1 = v; t.i1 = j; }
+        else if (v > t.v2) t.v2 = v;
+    };
+    const bool aligned16 = (reinterpret_cast<uintptr_t>(l) & 15) == 0;
+    if (aligned16) {
+        for (int64_t vi = v0 + threadIdx.x; vi < v1; vi += blockDim.x) {
+            const uint4 u = *reinterpret_cast<const uint4*>(l + vi * V);
+            const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+            for (int j = 0; j < V; ++j) consider(Act<T>::load(e[j]), vi * V + j);
+        }
+    } else {
+        for (int64_t j = v0 * V + threadIdx.x; j < v1 * V; j += blockDim.x) consider(Act<T>::load(l[j]), j);
+    }
+    if (blockIdx.x == gridDim.x - 1)  // ragged tail (vocab % V)
+        for (int64_t j = nvec * V + threadIdx.x; j < vocab; j += blockDim.x) consider(Act<T>::load(l[j]), j);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Top2 u;
+        u.v1 = __shfl_xor_sync(0xffffffffu, t.v1, o);
+        u.i1 = __shfl_xor_sync(0xffffffffu, t.i1, o);
+        u.v2 = __shfl_xor_sync(0xffffffffu, t.v2, o);
+        t = merge_top2(t, u);
+    }
+    __shared__ Top2 red[8];
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        Top2 b = red[0];
+        for (int w = 1; w < 8; ++w) b = merge_top2(b, red[w]);
+        parts[row * gridDim.x + blockIdx.x] = b;
+    }
+}
+
+__global__ void argmax_final_kernel(const Top2* __restrict__ parts, int nparts, int64_t* __restrict__ out_idx,
+                                    float* __restrict__ out_gap) {
+    const int64_t row = blockIdx.x;
+    Top2 t{-INFINITY, INT64_MAX, -INFINITY};
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) t = merge_top2(t, parts[row * nparts + i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Top2 u;
+        u.v1 = __shfl_xor_sync(0xffffffffu, t.v1, o);
+        u.i1 = __shfl_xor_sync(0xffffffffu, t.i1, o);
+        u.v2 = __shfl_xor_sync(0xffffffffu, t.v2, o);
+        t = merge_top2(t, u);
+    }
+    if (threadIdx.x == 0) {
+        out_idx[row] = t.i1 == INT64_MAX ? 0 : t.i1;
+        if (out_gap) out_gap[row] = t.v1 - t.v2;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Synthetic weights: integer-hash generators; the fp32 arithmetic is exact
 // except the final multiply and the fp16/bf16 conversion, all IEEE
@@ -324,6 +391,34 @@ am_status_code amcu_argmax(const void* logits, int64_t rows, int64_t vocab, int6
     else
         return set_error(AM_STATUS_INVALID_ARGUMENT, "amcu_argmax: dtype must be f32 or bf16");
     return check_launch("amcu_argmax");
+}
+
+size_t amcu_argmax_workspace_bytes(int64_t rows) {
+    return rows > 0 ? (size_t)rows * kArgmaxParts * sizeof(Top2) : 0;
+}
+
+am_status_code amcu_argmax_ws(const void* logits, int64_t rows, int64_t vocab, int64_t stride, int32_t dtype,
+                              int64_t* out_idx, float* out_gap, void* workspace, size_t workspace_size,
+                              void* stream) {
+    clear_error();
+    AMCU_REQUIRE(rows >= 0 && vocab > 0, "amcu_argmax_ws: bad sizes");
+    if (rows == 0) return AM_STATUS_OK;
+    AMCU_REQUIRE(logits && out_idx, "amcu_argmax_ws: null pointer");
+    if (stride == 0) stride = vocab;
+    AMCU_REQUIRE(stride >= vocab, "amcu_argmax_ws: row stride smaller than vocab");
+    AMCU_REQUIRE(workspace && workspace_size >= amcu_argmax_workspace_bytes(rows) && aligned(workspace, 16),
+                 "amcu_argmax_ws: workspace of %zu bytes (16-byte aligned) required", amcu_argmax_workspace_bytes(rows));
+    const dim3 grid(kArgmaxParts, (unsigned)rows);
+    Top2* parts = static_cast<Top2*>(workspace);
+    if (dtype == AMCU_F32)
+        argmax_partial_kernel<float><<<grid, 256, 0, as_stream(stream)>>>((const float*)logits, vocab, stride, parts);
+    else if (dtype == AMCU_BF16)
+        argmax_partial_kernel<__nv_bfloat16><<<grid, 256, 0, as_stream(stream)>>>((const __nv_bfloat16*)logits, vocab,
+                                                                                  stride, parts);
+    else
+        return set_error(AM_STATUS_INVALID_ARGUMENT, "amcu_argmax_ws: dtype must be f32 or bf16");
+    argmax_final_kernel<<<(unsigned)rows, 32, 0, as_stream(stream)>>>(parts, kArgmaxParts, out_idx, out_gap);
+    return check_launch("amcu_argmax_ws");
 }
 
 am_status_code amcu_synth_w4(uint64_t seed, uint64_t sid, int64_t n, int64_t k, float base, void* q, void* s,

@@ -13,52 +13,65 @@
 
 namespace amcu {
 
+__device__ __forceinline__ void rope_angle(double theta, int64_t d, int64_t pos, int64_t i, float& c, float& s) {
+    const double inv = 1.0 / pow(theta, 2.0 * (double)i / (double)d);
+    const double ang = (double)pos * inv;
+    c = (float)cos(ang);
+    s = (float)sin(ang);
+}
+
+__global__ void rope_table_kernel(double theta, int64_t d, int64_t max_pos, float2* table) {
+    const int64_t half = d / 2;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < max_pos * half;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        float c, s;
+        rope_angle(theta, d, e / half, e % half, c, s);
+        table[e] = make_float2(c, s);
+    }
+}
+
+// One CTA per (row, head); heads [0, nq) are query heads (rotated in place),
+// [nq, nq + nkv) key heads (rotated into the cache), the last nkv value
+// heads (copied into the cache). Thread i handles the pair (i, i + d/2).
 template <typename T>
-__global__ void __launch_bounds__(128) rope_kv_kernel(AmcuRopeKvArgs a) {
+__global__ void __launch_bounds__(64) rope_kv_kernel(AmcuRopeKvArgs a) {
     const int64_t row = blockIdx.x;
+    const int64_t head = blockIdx.y;
     const int64_t b = row / a.rows_per_seq;
     const int64_t pos = (int64_t)a.seq_pos[b] + row % a.rows_per_seq;
     const int64_t d = a.head_dim, half = d / 2;
     if (pos < 0 || pos >= a.capacity) {
-        if (a.status && threadIdx.x == 0) atomicExch(a.status, (int32_t)AM_STATUS_OUT_OF_RANGE);
+        if (a.status && threadIdx.x == 0 && head == 0) atomicExch(a.status, (int32_t)AM_STATUS_OUT_OF_RANGE);
         return;
     }
-    extern __shared__ float cs[];  // [half] cos, [half] sin
-    for (int64_t i = threadIdx.x; i < half; i += blockDim.x) {
-        const double inv = 1.0 / pow(a.theta, 2.0 * (double)i / (double)d);
-        const double ang = (double)pos * inv;
-        cs[i] = (float)cos(ang);
-        cs[half + i] = (float)sin(ang);
-    }
-    __syncthreads();
-    T* q = static_cast<T*>(a.q) + row * a.q_stride;
-    const T* k = static_cast<const T*>(a.k) + row * a.k_stride;
-    const T* v = static_cast<const T*>(a.v) + row * a.v_stride;
     const int64_t slot_stride = a.slot_stride ? a.slot_stride : a.n_kv_heads * a.capacity * d;
-    T* kc = static_cast<T*>(a.k_cache) + b * slot_stride + pos * d;
-    T* vc = static_cast<T*>(a.v_cache) + b * slot_stride + pos * d;
-    const int64_t nq = a.n_q_heads * half, nk = a.n_kv_heads * half;
-    for (int64_t e = threadIdx.x; e < nq + nk; e += blockDim.x) {
-        const bool is_q = e < nq;
-        const int64_t ee = is_q ? e : e - nq;
-        const int64_t h = ee / half, i = ee % half;
-        const T* src = is_q ? q + h * d : k + h * d;
+    const int64_t nq = a.n_q_heads, nkv = a.n_kv_heads;
+    if (head >= nq + nkv) {  // value head: copy
+        const int64_t h = head - nq - nkv;
+        const T* v = static_cast<const T*>(a.v) + row * a.v_stride + h * d;
+        T* vc = static_cast<T*>(a.v_cache) + b * slot_stride + (h * a.capacity + pos) * d;
+        for (int64_t i = threadIdx.x; i < d; i += blockDim.x) vc[i] = v[i];
+        return;
+    }
+    for (int64_t i = threadIdx.x; i < half; i += blockDim.x) {
+        float c, s;
+        if (a.cos_sin) {
+            const float2 v = reinterpret_cast<const float2*>(a.cos_sin)[pos * half + i];
+            c = v.x;
+            s = v.y;
+        } else {
+            rope_angle(a.theta, d, pos, i, c, s);
+        }
+        const bool is_q = head < nq;
+        const T* src = is_q ? static_cast<const T*>(a.q) + row * a.q_stride + head * d
+                            : static_cast<const T*>(a.k) + row * a.k_stride + (head - nq) * d;
         const float x1 = Act<T>::load(src[i]), x2 = Act<T>::load(src[i + half]);
-        const float c = cs[i], s = cs[half + i];
         const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
         const float o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
-        if (is_q) {
-            q[h * d + i] = Act<T>::store(o1);
-            q[h * d + i + half] = Act<T>::store(o2);
-        } else {
-            T* dst = kc + h * a.capacity * d;
-            dst[i] = Act<T>::store(o1);
-            dst[i + half] = Act<T>::store(o2);
-        }
-    }
-    for (int64_t e = threadIdx.x; e < a.n_kv_heads * d; e += blockDim.x) {
-        const int64_t h = e / d, i = e % d;
-        vc[h * a.capacity * d + i] = v[e];
+        T* dst = is_q ? static_cast<T*>(a.q) + row * a.q_stride + head * d
+                      : static_cast<T*>(a.k_cache) + b * slot_stride + ((head - nq) * a.capacity + pos) * d;
+        dst[i] = Act<T>::store(o1);
+        dst[i + half] = Act<T>::store(o2);
     }
 }
 
@@ -78,12 +91,25 @@ extern "C" am_status_code amcu_rope_kv_write(const AmcuRopeKvArgs* a, void* stre
     AMCU_REQUIRE(a->rows_per_seq > 0, "amcu_rope_kv_write: rows_per_seq must be positive");
     AMCU_REQUIRE(a->capacity > 0, "amcu_rope_kv_write: capacity must be positive");
     AMCU_REQUIRE(a->theta > 0.0, "amcu_rope_kv_write: theta must be positive");
-    const size_t smem = sizeof(float) * a->head_dim;
+    const dim3 grid((unsigned)a->rows, (unsigned)(a->n_q_heads + 2 * a->n_kv_heads));
     if (a->dtype == AMCU_F32)
-        rope_kv_kernel<float><<<(unsigned)a->rows, 128, smem, as_stream(stream)>>>(*a);
+        rope_kv_kernel<float><<<grid, 64, 0, as_stream(stream)>>>(*a);
     else if (a->dtype == AMCU_BF16)
-        rope_kv_kernel<__nv_bfloat16><<<(unsigned)a->rows, 128, smem, as_stream(stream)>>>(*a);
+        rope_kv_kernel<__nv_bfloat16><<<grid, 64, 0, as_stream(stream)>>>(*a);
     else
         return set_error(AM_STATUS_INVALID_ARGUMENT, "amcu_rope_kv_write: dtype must be f32 or bf16");
     return check_launch("amcu_rope_kv_write");
+}
+
+extern "C" am_status_code amcu_rope_table(double theta, int64_t head_dim, int64_t max_pos, float* table, void* stream) {
+    clear_error();
+    AMCU_REQUIRE(table && head_dim > 0 && head_dim % 2 == 0 && max_pos > 0 && theta > 0.0,
+                 "amcu_rope_table: bad arguments");
+    AMCU_REQUIRE(aligned(table, 8), "amcu_rope_table: table must be 8-byte aligned");
+    const int64_t n = max_pos * (head_dim / 2);
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    rope_table_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(theta, head_dim, max_pos,
+                                                                       reinterpret_cast<float2*>(table));
+    return check_launch("amcu_rope_table");
 }

@@ -79,6 +79,10 @@ Status BuildLinear(std::span<const TensorView> in, std::span<const MutableTensor
     a->y_stride = out[0].strides[0];
     a->act_dtype = AmDtype(in[0].dtype);
     a->epilogue = at ? at->epilogue : AMCU_EPI_STORE;
+    if (at) {
+        a->norm_weight = at->norm_weight;
+        a->norm_eps = at->norm_eps;
+    }
     if (in.size() > 1) a->residual = in[1].data;
     return Status::Ok();
 }
@@ -133,6 +137,7 @@ Status BuildRopeKv(std::span<const TensorView> in, std::span<const MutableTensor
     a->theta = at->theta;
     a->dtype = AmDtype(in[0].dtype);
     a->status = at->status;
+    a->cos_sin = at->cos_sin;
     return Status::Ok();
 }
 Status RopeKvFn(const KernelContext& c) noexcept {
@@ -245,6 +250,9 @@ Status BuildArgmax(std::span<const TensorView> in, std::span<const MutableTensor
 }
 Status ArgmaxFn(const KernelContext& c) noexcept {
     auto* a = static_cast<const ArgmaxArgs*>(c.kernel_params);
+    if (c.workspace_binding.data)
+        return FromAm(amcu_argmax_ws(a->logits, a->rows, a->vocab, a->stride, a->dtype, a->out, a->gap,
+                                     c.workspace_binding.data, c.workspace_binding.size, S(c)));
     return FromAm(amcu_argmax(a->logits, a->rows, a->vocab, a->stride, a->dtype, a->out, a->gap, S(c)));
 }
 

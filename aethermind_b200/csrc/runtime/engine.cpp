@@ -4,6 +4,7 @@
 
 #include <dlfcn.h>
 
+#include <cstdlib>
 #include <cstring>
 
 namespace aethermind {
@@ -228,8 +229,30 @@ Status LayerRunner::RunStep(const ExecutionPlan& plan, size_t i, Stream& stream,
     return s;
 }
 
+// AM_STEP_CHECK=1: synchronize after every step and report the first step
+// whose kernel failed (diagnostics; never inside a stream capture).
+static bool StepCheckEnabled() {
+    static const bool on = [] {
+        const char* e = getenv("AM_STEP_CHECK");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
 Status LayerRunner::Run(const ExecutionPlan& plan, Stream& stream, WorkspaceArena* ws, const KVCacheView* kv) const {
-    for (size_t i = 0; i < plan.steps.size(); ++i) AM_RETURN_IF_ERROR(RunStep(plan, i, stream, ws, kv));
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    const bool check = StepCheckEnabled() && cudaStreamIsCapturing(stream.handle(), &cap) == cudaSuccess &&
+                       cap == cudaStreamCaptureStatusNone;
+    for (size_t i = 0; i < plan.steps.size(); ++i) {
+        AM_RETURN_IF_ERROR(RunStep(plan, i, stream, ws, kv));
+        if (check) {
+            cudaError_t e = cudaStreamSynchronize(stream.handle());
+            if (e == cudaSuccess) e = cudaGetLastError();
+            if (e != cudaSuccess)
+                return Status::Internal("step " + std::to_string(i) + " (" + plan.steps[i].label +
+                                        "): " + cudaGetErrorString(e));
+        }
+    }
     return Status::Ok();
 }
 

@@ -84,6 +84,15 @@ struct am_model_s {
 namespace aethermind {
 namespace {
 
+// Host -> device copy ordered on the engine's stream and complete on return.
+// (A plain cudaMemcpy from pageable memory may return before its DMA lands,
+// and the engine's non-blocking stream is not ordered after it.)
+cudaError_t UploadSync(am_model_s* m, void* dst, const void* src, size_t bytes) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, m->rt->stream);
+    if (e != cudaSuccess) return e;
+    return cudaStreamSynchronize(m->rt->stream);
+}
+
 int64_t WeightBytes(const am_model_config_t& c, int64_t n, int64_t k) {
     return amcu_packed_weight_bytes(c.weight_format, c.act_dtype, n, k, c.group_size);
 }
@@ -195,11 +204,11 @@ Status UploadCanon(am_model_s* m, int64_t n, int64_t k, const void* hq, const vo
     out.n = n;
     out.k = k;
     AM_RETURN_IF_ERROR(AllocVec(m, out.q, RowBytes(c, k) * n));
-    AM_CUDA(cudaMemcpy(out.q.data(), hq, RowBytes(c, k) * n, cudaMemcpyHostToDevice));
+    AM_CUDA(UploadSync(m, out.q.data(), hq, RowBytes(c, k) * n));
     if (c.weight_format != AMCU_WFMT_PLAIN) {
         if (!hs) return Status::InvalidArgument("quantized weight needs scales");
         AM_RETURN_IF_ERROR(AllocVec(m, out.s, ScaleRowBytes(c, k) * n));
-        AM_CUDA(cudaMemcpy(out.s.data(), hs, ScaleRowBytes(c, k) * n, cudaMemcpyHostToDevice));
+        AM_CUDA(UploadSync(m, out.s.data(), hs, ScaleRowBytes(c, k) * n));
     }
     return Status::Ok();
 }
@@ -295,6 +304,7 @@ struct am_session_s {
     aethermind::Executor exec;
     aethermind::DeviceBuffer tokens, next_tok, seq_pos, counter, out_tokens, gaps, gap_tmp, status;
     aethermind::DeviceBuffer x, h, qkv, attn, act, part, hlast, logits;
+    aethermind::DeviceBuffer rope_table;  // [max_seq][head_dim/2] (cos, sin)
     int64_t rows_cap = 0, out_cap = 0;
     // plans
     aethermind::ExecutionPlan prefill, decode;
@@ -375,6 +385,8 @@ struct PlanBuilder {
         // workspace needs
         if (op == OpType::kLinear) {
             st.workspace_size = amcu_linear_workspace_bytes(reinterpret_cast<const AmcuLinearArgs*>(st.params.data()));
+        } else if (op == OpType::kArgmax) {
+            st.workspace_size = amcu_argmax_workspace_bytes(in.begin()->dim(0));  // one partial set per row
         } else if (op == OpType::kAttention && phase == ExecPhase::kDecode) {
             st.workspace_size =
                     amcu_attention_workspace_bytes(reinterpret_cast<const AmcuAttentionArgs*>(st.params.data()));
@@ -412,6 +424,9 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
     const KernelSelector lin = pb.Sel(A, wdt, wf);
     const KernelSelector act = pb.Sel(A, A, WeightFormat::kPlain);
     const bool tp = m->rt->tp_size > 1;
+    // Decode GEMVs (m <= 8) stage their activations anyway: the RMSNorm in
+    // front of q/k/v and gate/up runs there instead of as its own kernel.
+    const bool fuse_norm = phase == ExecPhase::kDecode && wf != WeightFormat::kPlain && M <= 8;
     s->ar_ctx.clear();
 
     // Embedding
@@ -427,16 +442,25 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
     for (int64_t l = 0; l < c.layers; ++l) {
         auto& L = m->layers[l];
         const std::string p = "layer" + std::to_string(l) + ".";
-        AM_RETURN_IF_ERROR(pb.Add(OpType::kRmsNorm, act, {View2(s->x.data(), A, M, H, H), MakeView(L.attn_norm.data(), A, {H})},
-                                  {MView2(s->h.data(), A, M, H, H)}, &na, nullptr, p + "attn_norm"));
         LinearAttrs store{AMCU_EPI_STORE};
-        AM_RETURN_IF_ERROR(pb.Add(OpType::kLinear, lin, {View2(s->h.data(), A, M, H, H)},
-                                  {MView2(s->qkv.data(), A, M, m->qkv_n, m->qkv_n)}, &store, &L.qkv.w, p + "qkv_proj"));
+        if (fuse_norm) {  // attn_norm folded into the q/k/v GEMV's activation staging
+            LinearAttrs qa{AMCU_EPI_STORE, L.attn_norm.data(), c.rms_eps};
+            AM_RETURN_IF_ERROR(pb.Add(OpType::kLinear, lin, {View2(s->x.data(), A, M, H, H)},
+                                      {MView2(s->qkv.data(), A, M, m->qkv_n, m->qkv_n)}, &qa, &L.qkv.w,
+                                      p + "attn_norm+qkv_proj"));
+        } else {
+            AM_RETURN_IF_ERROR(pb.Add(OpType::kRmsNorm, act,
+                                      {View2(s->x.data(), A, M, H, H), MakeView(L.attn_norm.data(), A, {H})},
+                                      {MView2(s->h.data(), A, M, H, H)}, &na, nullptr, p + "attn_norm"));
+            AM_RETURN_IF_ERROR(pb.Add(OpType::kLinear, lin, {View2(s->h.data(), A, M, H, H)},
+                                      {MView2(s->qkv.data(), A, M, m->qkv_n, m->qkv_n)}, &store, &L.qkv.w,
+                                      p + "qkv_proj"));
+        }
         const int64_t qn = m->nq_l * d, kn = m->nkv_l * d;
         char* qkv = s->qkv.as<char>();
         RopeKvAttrs ra{c.rope_theta, R, (int64_t)s->kv.layout().max_tokens,
                        (int64_t)(s->kv.layout().slot_stride / e), m->nq_l, m->nkv_l, d, s->seq_pos.as<int32_t>(),
-                       s->status.as<int32_t>()};
+                       s->status.as<int32_t>(), s->rope_table.as<float>()};
         TensorView q = View2(qkv, A, M, qn, m->qkv_n), k = View2(qkv + qn * e, A, M, kn, m->qkv_n),
                    v = View2(qkv + (qn + kn) * e, A, M, kn, m->qkv_n);
         MutableTensorView qo = MView2(qkv, A, M, qn, m->qkv_n);
@@ -468,11 +492,20 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
                           {MView2(s->x.data(), A, M, H, H)}, (const int*)nullptr, nullptr, p + name + "_residual");
         };
         AM_RETURN_IF_ERROR(residual_block(L.o, View2(s->attn.data(), A, M, qn, qn), "o_proj"));
-        AM_RETURN_IF_ERROR(pb.Add(OpType::kRmsNorm, act, {View2(s->x.data(), A, M, H, H), MakeView(L.mlp_norm.data(), A, {H})},
-                                  {MView2(s->h.data(), A, M, H, H)}, &na, nullptr, p + "mlp_norm"));
-        LinearAttrs silu{AMCU_EPI_SILU_MUL};
-        AM_RETURN_IF_ERROR(pb.Add(OpType::kLinear, lin, {View2(s->h.data(), A, M, H, H)},
-                                  {MView2(s->act.data(), A, M, m->inter_l, m->inter_l)}, &silu, &L.gu.w, p + "gate_up_silu"));
+        if (fuse_norm) {  // mlp_norm folded into the gate/up GEMV's activation staging
+            LinearAttrs silu{AMCU_EPI_SILU_MUL, L.mlp_norm.data(), c.rms_eps};
+            AM_RETURN_IF_ERROR(pb.Add(OpType::kLinear, lin, {View2(s->x.data(), A, M, H, H)},
+                                      {MView2(s->act.data(), A, M, m->inter_l, m->inter_l)}, &silu, &L.gu.w,
+                                      p + "mlp_norm+gate_up_silu"));
+        } else {
+            AM_RETURN_IF_ERROR(pb.Add(OpType::kRmsNorm, act,
+                                      {View2(s->x.data(), A, M, H, H), MakeView(L.mlp_norm.data(), A, {H})},
+                                      {MView2(s->h.data(), A, M, H, H)}, &na, nullptr, p + "mlp_norm"));
+            LinearAttrs silu{AMCU_EPI_SILU_MUL};
+            AM_RETURN_IF_ERROR(pb.Add(OpType::kLinear, lin, {View2(s->h.data(), A, M, H, H)},
+                                      {MView2(s->act.data(), A, M, m->inter_l, m->inter_l)}, &silu, &L.gu.w,
+                                      p + "gate_up_silu"));
+        }
         AM_RETURN_IF_ERROR(residual_block(L.d, View2(s->act.data(), A, M, m->inter_l, m->inter_l), "down_proj"));
     }
     // final norm on the last row of every sequence
@@ -568,27 +601,32 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
     AM_CUDA(cudaStreamSynchronize(st));
 
     const bool use_graph = s->cfg.use_cuda_graph != 0;
-    if (use_graph && N > 1 && s->graph_B != B) {
-        cudaGraph_t g = nullptr;
-        AM_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-        Status cs = s->exec.Execute(s->decode, stream, &s->ws, &kv);
-        if (cs.ok()) cs = RunAdvance(s, B, -1, st);
-        cudaError_t ce = cudaStreamEndCapture(st, &g);
-        AM_RETURN_IF_ERROR(cs);
-        AM_CUDA(ce);
-        cudaGraphExec_t ge = nullptr;
-        cudaError_t ie = cudaGraphInstantiate(&ge, g, 0);
-        cudaGraphDestroy(g);
-        AM_CUDA(ie);
-        s->graph = ge;
-        s->graph_B = B;
-    }
     for (int64_t i = 1; i < N; ++i) {
-        if (use_graph) {
+        if (use_graph && s->graph_B == B) {
             AM_CUDA(cudaGraphLaunch(s->graph, st));
-        } else {
-            AM_RETURN_IF_ERROR(s->exec.Execute(s->decode, stream, &s->ws, &kv));
-            AM_RETURN_IF_ERROR(RunAdvance(s, B, -1, st));
+            continue;
+        }
+        // Eager decode step. The first one also loads every decode kernel's
+        // module (CUDA loads modules lazily, on first launch), so nothing is
+        // loaded while the decode graph is being captured below.
+        AM_RETURN_IF_ERROR(s->exec.Execute(s->decode, stream, &s->ws, &kv));
+        AM_RETURN_IF_ERROR(RunAdvance(s, B, -1, st));
+        if (use_graph && i + 1 < N) {
+            AM_CUDA(cudaStreamSynchronize(st));
+            cudaGraph_t g = nullptr;
+            AM_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+            Status cs = s->exec.Execute(s->decode, stream, &s->ws, &kv);
+            if (cs.ok()) cs = RunAdvance(s, B, -1, st);
+            cudaError_t ce = cudaStreamEndCapture(st, &g);
+            AM_RETURN_IF_ERROR(cs);
+            AM_CUDA(ce);
+            cudaGraphExec_t ge = nullptr;
+            cudaError_t ie = cudaGraphInstantiate(&ge, g, 0);
+            cudaGraphDestroy(g);
+            AM_CUDA(ie);
+            s->graph = ge;
+            s->graph_B = B;
+            AM_CUDA(cudaGraphUpload(ge, st));
         }
     }
     AM_CUDA(cudaEventRecord(s->ev[2], st));
@@ -756,7 +794,7 @@ static Status FillOnes(am_model_s* m, DeviceBuffer& b, int64_t n) {
         uint16_t* u = reinterpret_cast<uint16_t*>(host.data());
         for (int64_t i = 0; i < n; ++i) u[i] = 0x3F80;  // bf16 1.0
     }
-    return CudaOk(cudaMemcpy(b.data(), host.data(), host.size(), cudaMemcpyHostToDevice), "norm upload");
+    return CudaOk(UploadSync(m, b.data(), host.data(), host.size()), "norm upload");
 }
 
 am_status_code am_model_init_synthetic(am_model_t m, uint64_t seed) {
@@ -816,7 +854,7 @@ am_status_code am_model_set_weight(am_model_t m, const char* name_c, const void*
         if (name == "embed") {
             if (c.tied_embeddings && c.weight_format == AMCU_WFMT_INT8)
                 throw Status::InvalidArgument("tied int8 model: set 'lm_head' (it also feeds the embedding)");
-            chk(CudaOk(cudaMemcpy(m->embed.data(), data, c.vocab * c.hidden * e, cudaMemcpyHostToDevice), "embed"));
+            chk(CudaOk(UploadSync(m, m->embed.data(), data, c.vocab * c.hidden * e), "embed"));
             if (c.tied_embeddings) {  // tied plain: the lm_head is the same matrix
                 Canon full;
                 chk(UploadCanon(m, c.vocab, c.hidden, data, scales, full));
@@ -826,12 +864,12 @@ am_status_code am_model_set_weight(am_model_t m, const char* name_c, const void*
             Canon full;
             chk(UploadCanon(m, c.vocab, c.hidden, data, scales, full));
             if (c.tied_embeddings && c.weight_format == AMCU_WFMT_INT8) {
-                chk(CudaOk(cudaMemcpy(m->embed.data(), data, c.vocab * c.hidden, cudaMemcpyHostToDevice), "embed"));
-                chk(CudaOk(cudaMemcpy(m->embed_scales.data(), scales, c.vocab * 4, cudaMemcpyHostToDevice), "embed"));
+                chk(CudaOk(UploadSync(m, m->embed.data(), data, c.vocab * c.hidden), "embed"));
+                chk(CudaOk(UploadSync(m, m->embed_scales.data(), scales, c.vocab * 4), "embed"));
             }
             chk(PackInto(m, m->lm_head, 0, full));
         } else if (name == "final_norm") {
-            chk(CudaOk(cudaMemcpy(m->final_norm.data(), data, c.hidden * e, cudaMemcpyHostToDevice), "norm"));
+            chk(CudaOk(UploadSync(m, m->final_norm.data(), data, c.hidden * e), "norm"));
         } else if (name.rfind("layers.", 0) == 0) {
             const size_t dot = name.find('.', 7);
             if (dot == std::string::npos) throw Status::NotFound("bad weight name " + name);
@@ -840,8 +878,7 @@ am_status_code am_model_set_weight(am_model_t m, const char* name_c, const void*
             const std::string t = name.substr(dot + 1);
             auto& L = m->layers[l];
             if (t == "attn_norm" || t == "mlp_norm") {
-                chk(CudaOk(cudaMemcpy((t == "attn_norm" ? L.attn_norm : L.mlp_norm).data(), data, c.hidden * e,
-                                      cudaMemcpyHostToDevice), "norm"));
+                chk(CudaOk(UploadSync(m, (t == "attn_norm" ? L.attn_norm : L.mlp_norm).data(), data, c.hidden * e), "norm"));
             } else {
                 Target tg;
                 chk(ResolveTarget(m, l, t, tg));
@@ -885,6 +922,12 @@ am_session_t am_session_create(am_model_t m, const am_session_config_t* cfg) {
     get(s->status, 16);
     get(s->hlast, c.max_batch * c.hidden * DTypeBytes(m->act));
     get(s->logits, c.max_batch * c.vocab * DTypeBytes(m->act));
+    get(s->rope_table, c.max_seq * (c.head_dim / 2) * 8);
+    if (st.ok())
+        st = Status::FromAm(amcu_rope_table(c.rope_theta, c.head_dim, c.max_seq, s->rope_table.as<float>(),
+                                            m->rt->stream),
+                            amcu_last_error());
+    if (st.ok()) st = CudaOk(cudaStreamSynchronize(m->rt->stream), "rope table");
     if (!st.ok()) {
         g_err = st.ToString();
         delete s;

@@ -9,13 +9,16 @@ struct RmsNormAttrs {
     float eps;
 };
 struct LinearAttrs {
-    int32_t epilogue;  // amcu_epilogue
+    int32_t epilogue;                  // amcu_epilogue
+    const void* norm_weight = nullptr;  // fused RMSNorm of the input (decode GEMV)
+    float norm_eps = 0.f;
 };
 struct RopeKvAttrs {
     double theta;
     int64_t rows_per_seq, capacity, slot_stride, n_q, n_kv, head_dim;
     const int32_t* seq_pos;
     int32_t* status;
+    const float* cos_sin = nullptr;  // precomputed table (amcu_rope_table)
 };
 struct AttentionAttrs {
     int64_t rows_per_seq, capacity, slot_stride, n_q, n_kv, head_dim, max_context;

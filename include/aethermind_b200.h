@@ -195,6 +195,9 @@ typedef struct AmcuLinearArgs {
     int32_t epilogue;       /* amcu_epilogue */
     void* workspace;        /* device scratch (prefill GEMM); may be NULL for m <= 8 */
     size_t workspace_size;
+    const void* norm_weight; /* optional: x is first RMS-normalized with this [k] weight
+                                (the RMSNorm that precedes q/k/v and gate/up, fused) */
+    float norm_eps;
 } AmcuLinearArgs;
 /* Dispatches on m: GEMV (m <= 8) or the tensor-core GEMM (m > 8). */
 am_status_code amcu_linear(const AmcuLinearArgs* args, void* stream);
@@ -232,8 +235,13 @@ typedef struct AmcuRopeKvArgs {
     double theta;
     int32_t dtype;           /* AMCU_F32 / AMCU_BF16 (activations and cache) */
     int32_t* status;         /* optional device word: set to AM_STATUS_OUT_OF_RANGE on a position >= capacity */
+    const float* cos_sin;    /* optional table from amcu_rope_table (same values, no per-token trig) */
 } AmcuRopeKvArgs;
 am_status_code amcu_rope_kv_write(const AmcuRopeKvArgs* args, void* stream);
+/* cos/sin table for positions [0, max_pos): table[pos][i] = (cos, sin) of
+ * pos * theta^(-2i/head_dim), i < head_dim/2, computed in double and rounded
+ * to float exactly as amcu_rope_kv_write does on the fly. 8*max_pos*(head_dim/2) bytes. */
+am_status_code amcu_rope_table(double theta, int64_t head_dim, int64_t max_pos, float* table, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* GQA attention over the static KV cache (reference InferAttention,          */
@@ -283,6 +291,12 @@ am_status_code amcu_add(const void* a, const void* b, void* out, int64_t count, 
 /* ------------------------------------------------------------------------ */
 am_status_code amcu_argmax(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
                            int32_t dtype, int64_t* out_index, float* out_gap, void* stream);
+/* Same result, split over many CTAs per row (for vocabularies of 10^5):
+ * needs a device workspace of amcu_argmax_workspace_bytes(rows) bytes. */
+size_t amcu_argmax_workspace_bytes(int64_t rows);
+am_status_code amcu_argmax_ws(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                              int32_t dtype, int64_t* out_index, float* out_gap, void* workspace,
+                              size_t workspace_size, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Embedding gather (src/backend/cpu/kernels/embedding/embedding_entry.cpp:  */

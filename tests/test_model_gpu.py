@@ -16,7 +16,8 @@ pytestmark = pytest.mark.gpu
 def _compare(got, ref, gaps, tie):
     for i, (a, b) in enumerate(zip(got, ref)):
         if a != b:
-            assert gaps[i] < tie, f"token {i}: {a} != {b} with oracle gap {gaps[i]:.4g} >= {tie}"
+            assert gaps[i] < tie, (f"token {i}: {a} != {b} with oracle gap {gaps[i]:.4g} >= {tie}; "
+                                   f"engine {list(got)[:12]} oracle {list(ref)[:12]}")
             return i
     return len(ref)
 

@@ -22,6 +22,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "kernels/decode_state.cuh"
 #include "runtime/engine.h"
 
@@ -592,6 +594,11 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
     AM_CUDA(cudaMemsetAsync(s->counter.data(), 0, 4, st));
     AM_CUDA(cudaMemsetAsync(s->status.data(), 0, 4, st));
     AM_CUDA(cudaEventRecord(s->ev[0], st));
+    struct NvtxRange {  // named ranges for profilers (am_prefill / am_decode)
+        explicit NvtxRange(const char* n) { nvtxRangePushA(n); }
+        ~NvtxRange() { nvtxRangePop(); }
+    };
+    std::unique_ptr<NvtxRange> range = std::make_unique<NvtxRange>("am_prefill");
     AM_RETURN_IF_ERROR(s->exec.Execute(s->prefill, stream, &s->ws, &kv));
     AM_RETURN_IF_ERROR(RunAdvance(s, B, (int32_t)P, st));
     AM_CUDA(cudaEventRecord(s->ev[1], st));
@@ -601,6 +608,8 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
     AM_CUDA(cudaStreamSynchronize(st));
 
     const bool use_graph = s->cfg.use_cuda_graph != 0;
+    range.reset();
+    range = std::make_unique<NvtxRange>("am_decode");
     for (int64_t i = 1; i < N; ++i) {
         if (use_graph && s->graph_B == B) {
             AM_CUDA(cudaGraphLaunch(s->graph, st));
@@ -630,6 +639,7 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
         }
     }
     AM_CUDA(cudaEventRecord(s->ev[2], st));
+    range.reset();
     int64_t* ho = hp + B * P;
     float* hg = reinterpret_cast<float*>(ho + c.max_batch * s->out_cap);
     AM_CUDA(cudaMemcpyAsync(ho, s->out_tokens.data(), B * s->out_cap * 8, cudaMemcpyDeviceToHost, st));

@@ -148,28 +148,20 @@ def decode_bytes_per_token(cfg, ctx: float) -> float:
     return w + kv
 
 
-def cpu_oracle_decode(cfg, prompt_len: int, new: int, layers: int | None = None) -> dict:
+def cpu_oracle_model(cfg):
+    import oracle
+    return oracle.synthetic_oracle_model(cfg, SEED)
+
+
+def cpu_oracle_decode(om, cfg, prompt_len: int, new: int) -> dict:
     """Greedy decode of the synthetic model by the CPU oracle; returns tok/s of
     the decode phase (all host threads via OpenMP)."""
     import numpy as np
 
-    import oracle
-
-    t0 = time.time()
-    om = oracle.synthetic_oracle_model(cfg, SEED, layers=layers)
-    if layers is not None:
-        om.m.layers = layers
-    gen_s = time.time() - t0
     prompt = np.random.default_rng(SEED).integers(0, cfg.vocab, prompt_len).astype(np.int64)
-    t1 = time.time()
-    om.generate(prompt, 1)
-    t_prefill = time.time() - t1
-    t2 = time.time()
     om.generate(prompt, 1 + new)
-    t_total = time.time() - t2
-    dec = max(t_total - t_prefill, 1e-9)
-    return {"tok_s": new / dec, "prefill_s": t_prefill, "weights_gen_s": gen_s,
-            "cores": os.cpu_count()}
+    t_prefill, t_decode = om.last_timing()
+    return {"tok_s": new / max(t_decode, 1e-9), "prefill_s": t_prefill, "cores": os.cpu_count()}
 
 
 def run_reference(args) -> None:
@@ -179,9 +171,10 @@ def run_reference(args) -> None:
     from aethermind_b200.session import LLAMA_8B_W4
     import dataclasses
     cfg = dataclasses.replace(LLAMA_8B_W4, max_seq=PROMPT + NEW)
+    om = cpu_oracle_model(cfg)
     steps = []
     for _ in range(args.warmup + args.steps):
-        steps.append(cpu_oracle_decode(cfg, 8, 2))
+        steps.append(cpu_oracle_decode(om, cfg, 8, 2))
     timed = steps[args.warmup:]
     v = statistics.mean(s["tok_s"] for s in timed)
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
@@ -305,7 +298,8 @@ def main() -> None:
         line["roofline"] = gemv_roofline(hbm_peak)
         line["roofline"]["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cb = cpu_oracle_decode(dataclasses.replace(cfg, max_seq=64), 8, 2)
+        ccfg = dataclasses.replace(cfg, max_seq=64)
+        cb = cpu_oracle_decode(cpu_oracle_model(ccfg), ccfg, 8, 2)
         line["cpu_baseline"] = {"value": round(cb["tok_s"], 4), "unit": "tok/s", "cores": cb["cores"], "kind": "port",
                                 "sample": "8-token prompt + 2 greedy decode tokens of the same 32-layer 8B W4 "
                                           "synthetic model (oracle/am_oracle.c, OpenMP on all host threads)"}

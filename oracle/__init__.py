@@ -80,6 +80,7 @@ def orc() -> C.CDLL:
             "orc_kv_write": (None, [P, P, P, P, i64, i64, i64, i64, i64]),
             "orc_attention": (None, [P, P, P, P, i64, i64, i64, i64, i64, i64, C.c_int]),
             "orc_generate": (i64, [C.POINTER(OrcModel), P, i64, i64, P, P, P]),
+            "orc_last_timing": (None, [C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         }
         for n, (r, a) in sig.items():
             f = getattr(l, n)
@@ -267,6 +268,13 @@ class OracleModel:
         gaps = np.zeros(max_new, np.float32)
         n = orc().orc_generate(C.byref(self.m), _p(p), p.size, max_new, _p(out), None, _p(gaps))
         return out[:n], gaps[:n]
+
+    @staticmethod
+    def last_timing() -> tuple[float, float]:
+        """(prefill seconds, decode seconds) of the last generate call."""
+        a, b = C.c_double(), C.c_double()
+        orc().orc_last_timing(C.byref(a), C.byref(b))
+        return a.value, b.value
 
 
 # same float32 arithmetic as the engine's constants (0.02f / 4.6098f, 0.02f / 73.61f)

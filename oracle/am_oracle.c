@@ -392,6 +392,15 @@ static void forward_chunk(const orc_model* m, const int64_t* ids, int64_t M, int
     free(x); free(h); free(q); free(k); free(v); free(a); free(o); free(g); free(u); free(posv);
 }
 
+#include <omp.h>
+static double now_s(void) { return omp_get_wtime(); }
+static double g_prefill_s = 0.0, g_decode_s = 0.0;
+/* Wall time of the prefill and of the decode steps of the last orc_generate. */
+void orc_last_timing(double* prefill_s, double* decode_s) {
+    *prefill_s = g_prefill_s;
+    *decode_s = g_decode_s;
+}
+
 int64_t orc_generate(const orc_model* m, const int64_t* prompt, int64_t P, int64_t max_new,
                      int64_t* out, float* last_logits, float* gaps) {
     const size_t plane = (size_t)m->nkv * m->max_seq * m->hd;
@@ -400,7 +409,10 @@ int64_t orc_generate(const orc_model* m, const int64_t* prompt, int64_t P, int64
     float* logits = (float*)malloc(sizeof(float) * m->vocab);
     int64_t n = 0;
     if (P + max_new > m->max_seq) max_new = m->max_seq - P;
+    double t0 = now_s();
     forward_chunk(m, prompt, P, 0, kc, vc, logits);
+    g_prefill_s = now_s() - t0;
+    t0 = now_s();
     for (n = 0; n < max_new; ++n) {
         int64_t t = orc_argmax(logits, m->vocab);
         if (gaps) {
@@ -413,6 +425,7 @@ int64_t orc_generate(const orc_model* m, const int64_t* prompt, int64_t P, int64
         if (n + 1 == max_new) break;
         forward_chunk(m, &out[n], 1, P + n, kc, vc, logits);
     }
+    g_decode_s = now_s() - t0;
     if (last_logits) memcpy(last_logits, logits, sizeof(float) * m->vocab);
     free(kc); free(vc); free(logits);
     return max_new > 0 ? n + 1 : 0;

@@ -103,6 +103,9 @@ int64_t orc_generate(const orc_model* m, const int64_t* prompt, int64_t prompt_l
                      int64_t max_new, int64_t* out_tokens, float* last_logits_out,
                      float* top2_gap_out);
 
+/* Wall time (s) of the prefill and of the decode steps of the last orc_generate. */
+void orc_last_timing(double* prefill_s, double* decode_s);
+
 #ifdef __cplusplus
 }
 #endif

@@ -122,6 +122,7 @@ _SIGS = {
     "amcu_attention_workspace_bytes": (C.c_size_t, [C.POINTER(AmcuAttentionArgs)]),
     "amcu_attn_decode": (C.c_int, [C.POINTER(AmcuAttentionArgs), P]),
     "amcu_attn_prefill": (C.c_int, [C.POINTER(AmcuAttentionArgs), P]),
+    "amcu_attn_decode_noalloc": (C.c_int, [C.POINTER(AmcuAttentionArgs), P]),
     "amcu_silu_mul": (C.c_int, [P, P, P, C.c_int64, C.c_int32, P]),
     "amcu_add": (C.c_int, [P, P, P, C.c_int64, C.c_int32, P]),
     "amcu_argmax": (C.c_int, [P, C.c_int64, C.c_int64, C.c_int64, C.c_int32, P, P, P]),

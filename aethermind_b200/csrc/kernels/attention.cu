@@ -12,6 +12,8 @@
 // P*V with lane l owning d/32 output dims (coalesced V rows). With one split
 // the CTA normalises and stores the output directly; with several it writes
 // (max, sum, unnormalised o) partials and a combine kernel merges them.
+#include <mutex>
+
 #include "../amcu_internal.h"
 #include "common.cuh"
 
@@ -492,3 +494,71 @@ am_status_code amcu_attn_prefill(const AmcuAttentionArgs* a, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode attention.
+//
+// Some callers cannot allocate device memory when they call into this
+// library. Examples: a serving process that carves up HBM once at start-up
+// and forbids allocations afterwards, or a latency-critical step in which
+// cudaMalloc's implicit device synchronization is not acceptable. Such
+// callers cannot provide the split-K workspace that amcu_attn_decode needs.
+// amcu_attn_decode_noalloc runs the same kernels with a fixed scratch buffer
+// that is compiled into the library instead.
+//
+// The scratch is a file-scope __device__ array of kNoAllocScratchBytes, so
+// every GPU that loads this library holds it until the process exits. In
+// host code the array's name only stands in for its device address. That
+// address is looked up once per device with cudaGetSymbolAddress, while that
+// device is current, on the first call made on that device.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoAllocScratchBytes];
+
+am_status_code noalloc_scratch(void** out) {
+    static void* addr[64] = {};
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(AM_STATUS_INTERNAL, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 64) return set_error(AM_STATUS_OUT_OF_RANGE, "device %d not supported", dev);
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            return set_error(AM_STATUS_INTERNAL, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+        }
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return AM_STATUS_OK;
+}
+
+}  // namespace
+
+extern "C" am_status_code amcu_attn_decode_noalloc(const AmcuAttentionArgs* a, void* stream) {
+    clear_error();
+    am_status_code st = validate_attn(a, "amcu_attn_decode_noalloc");
+    if (st != AM_STATUS_OK) return st;
+    if (a->rows == 0) return AM_STATUS_OK;
+    const int ns = choose_splits(a);
+    const size_t need = amcu_attention_workspace_bytes(a);
+    if (need > kNoAllocScratchBytes)
+        return set_error(AM_STATUS_INVALID_ARGUMENT,
+                         "amcu_attn_decode_noalloc: these sizes need %zu bytes of split scratch; the built-in scratch "
+                         "holds %zu (use fewer rows, heads or splits, or amcu_attn_decode with a workspace)",
+                         need, kNoAllocScratchBytes);
+    void* scratch = nullptr;
+    st = noalloc_scratch(&scratch);
+    if (st != AM_STATUS_OK) return st;
+    // Every split writes all of its partial (max, sum, output) before the
+    // combine reads it, so nothing in the scratch has to start at zero.
+    AmcuAttentionArgs b = *a;
+    b.workspace = scratch;
+    b.workspace_size = kNoAllocScratchBytes;
+    return run_attn(&b, ns, as_stream(stream));
+}

@@ -273,6 +273,19 @@ typedef struct AmcuAttentionArgs {
 size_t amcu_attention_workspace_bytes(const AmcuAttentionArgs* args);
 am_status_code amcu_attn_decode(const AmcuAttentionArgs* args, void* stream);
 am_status_code amcu_attn_prefill(const AmcuAttentionArgs* args, void* stream);
+/* Decode attention that allocates nothing (no counterpart in the reference).
+ * For callers that cannot allocate device memory while they run: a server
+ * that reserves all of HBM at start-up and forbids later allocations, or a
+ * latency-critical step where cudaMalloc's implicit synchronization is not
+ * acceptable. Same kernels and result as amcu_attn_decode; the split-K
+ * partials go to a 4 MiB scratch array built into the library (held on every
+ * GPU that loads it, until exit) instead of args->workspace (ignored).
+ * Sizes whose scratch (amcu_attention_workspace_bytes) exceeds 4 MiB are
+ * rejected with AM_STATUS_INVALID_ARGUMENT. The first call on a device looks
+ * up the scratch's device address; make that first call before any stream
+ * capture. All calls share the one scratch: calls that overlap on the GPU
+ * (e.g. on different streams) race and must be serialized by the caller. */
+am_status_code amcu_attn_decode_noalloc(const AmcuAttentionArgs* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* SiLU-Mul: out = round(silu(gate) * up), sign-branched fp32 SiLU            */

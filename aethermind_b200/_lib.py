@@ -6,9 +6,10 @@ Python or CPU fallback for any op.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "lib" / "libaethermind_b200.so"
+LIB_PATH = Path(os.environ.get("AMCU_LIB") or Path(__file__).resolve().parent / "lib" / "libaethermind_b200.so")
 
 # amcu_dtype
 F32, BF16, F16, I8, I4, I32, I64, U32 = range(8)
@@ -104,6 +105,8 @@ _SIGS = {
     "am_error_message": (C.c_char_p, [P]),
     "amcu_packed_weight_bytes": (C.c_int64, [C.c_int32, C.c_int32, C.c_int64, C.c_int64, C.c_int64]),
     "amcu_packed_scale_bytes": (C.c_int64, [C.c_int32, C.c_int64, C.c_int64, C.c_int64]),
+    "amcu_prepack_weight_rows": (C.c_int, [C.c_int32, C.c_int32, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
+                                           C.c_int64, P, P, P, P, P]),
     "amcu_prepack_weight": (C.c_int, [C.c_int32, C.c_int32, C.c_int64, C.c_int64, C.c_int64, P, P, P, P, P]),
     "amcu_unpack_weight": (C.c_int, [C.c_int32, C.c_int32, C.c_int64, C.c_int64, C.c_int64, P, P, P, P, P]),
     "amcu_prepack_gate_up": (C.c_int, [C.c_int32, C.c_int32, C.c_int64, C.c_int64, C.c_int64, P, P, P, P, P, P, P]),

@@ -29,6 +29,30 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 int num_sms();
+
+// Whether kernels of the hot path are launched with programmatic stream
+// serialization (on unless the environment sets AMCU_PDL=0; read once).
+bool pdl_enabled();
+
+// Launches `kernel` on `s` with the programmatic-stream-serialization
+// attribute when pdl_enabled(). The kernel must call pdl_wait() before it
+// touches memory that earlier kernels on the stream write or read. Launch
+// errors are left for check_launch() (cudaGetLastError).
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 // Per-device int32 error word that kernels with bounded waits write on timeout
 // (allocated on first use on the current device; nullptr if that fails).
 int32_t* device_error_word();

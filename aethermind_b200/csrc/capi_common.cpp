@@ -3,6 +3,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -32,6 +33,14 @@ int num_sms() {
     if (cudaGetDevice(&dev) != cudaSuccess) return 148;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
     return n;
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("AMCU_PDL");
+        return !(v && v[0] == '0');
+    }();
+    return on;
 }
 
 int32_t* device_error_word() {

@@ -58,6 +58,8 @@ struct AttnKParams {
 
 template <typename T, int GRP, int D>
 __global__ void __launch_bounds__(kAttnThreads) attn_splitk_kernel(AttnKParams p) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int NW = kAttnThreads / 32;
     constexpr int DL = D / 32;  // dims per lane in the P*V phase
     const int split = blockIdx.x, kvh = blockIdx.y;
@@ -185,6 +187,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_splitk_kernel(AttnKParams p
 // owning head_dim/32 output dims of every head (V rows read coalesced).
 template <typename T, int GRP, int D>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnKParams p) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int NW = kAttnThreads / 32;
     constexpr int DQ = D / 4;   // dims per lane in the QK phase
     constexpr int DL = D / 32;  // dims per lane in the PV phase
@@ -336,6 +340,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnKParams p
 constexpr int kMaxSplits = 64;
 template <typename T, int D>
 __global__ void __launch_bounds__(D) attn_combine_kernel(AttnKParams p) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x / p.nq, qh = blockIdx.x % p.nq;
     const float* w = p.ws + (row * p.nq + qh) * p.nsplit * (D + 2);
     __shared__ float f[kMaxSplits];
@@ -375,12 +381,12 @@ template <typename T, int GRP, int D>
 static void launch_attn(const AttnKParams& p, int64_t rows, cudaStream_t s) {
     const dim3 grid((unsigned)p.nsplit, (unsigned)p.nkv, (unsigned)rows);
     if constexpr (sizeof(T) == 2) {
-        if (p.rows_per_seq == 1) attn_decode_kernel<T, GRP, D><<<grid, kAttnThreads, 0, s>>>(p);
-        else attn_splitk_kernel<T, GRP, D><<<grid, kAttnThreads, 0, s>>>(p);
+        if (p.rows_per_seq == 1) launch_pdl(attn_decode_kernel<T, GRP, D>, grid, dim3(kAttnThreads), 0, s, p);
+        else launch_pdl(attn_splitk_kernel<T, GRP, D>, grid, dim3(kAttnThreads), 0, s, p);
     } else {
-        attn_splitk_kernel<T, GRP, D><<<grid, kAttnThreads, 0, s>>>(p);
+        launch_pdl(attn_splitk_kernel<T, GRP, D>, grid, dim3(kAttnThreads), 0, s, p);
     }
-    if (p.nsplit > 1) attn_combine_kernel<T, D><<<(unsigned)(rows * p.nq), D, 0, s>>>(p);
+    if (p.nsplit > 1) launch_pdl(attn_combine_kernel<T, D>, dim3((unsigned)(rows * p.nq)), dim3(D), 0, s, p);
 }
 
 template <typename T, int D>

@@ -124,6 +124,24 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// ---- programmatic dependent launch (PDL) ----
+// Kernels of the decode/prefill path are launched with programmatic stream
+// serialization (launch_pdl), so a kernel's CTAs may start while the kernel
+// before it on the stream is still running. Every such kernel calls pdl_wait()
+// before it reads or writes anything the earlier kernels produce or consume;
+// work that depends on nothing (weight prefetch) goes before it. pdl_wait
+// returns once all earlier kernels have completed and their writes are
+// visible, so chains stay ordered transitively. pdl_trigger() lets the next
+// kernel's CTAs be scheduled; without it they start at this kernel's exit.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Asks the TMA engine to pull [p, p + bytes) into L2 (no completion to wait
+// on). p 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Orderable 32-bit key of a float (total order matching float <, NaN last).
 __device__ __forceinline__ uint32_t float_order_key(float f) {
     uint32_t u = __float_as_uint(f);

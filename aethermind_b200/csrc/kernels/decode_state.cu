@@ -3,6 +3,7 @@
 // chosen token of every sequence is appended to the output buffer, its logit
 // gap is recorded, and the sequence position advances.
 #include "../amcu_internal.h"
+#include "common.cuh"
 #include "decode_state.cuh"
 
 namespace amcu {
@@ -10,6 +11,8 @@ namespace amcu {
 __global__ void advance_kernel(const int64_t* __restrict__ next, const float* __restrict__ gap, int64_t* out,
                                float* gaps_out, int64_t out_cap, int32_t* seq_pos, int32_t* counter,
                                int64_t batch, int32_t set_pos) {
+    pdl_wait();
+    pdl_trigger();
     const int idx = *counter;
     for (int64_t b = threadIdx.x; b < batch; b += blockDim.x) {
         if (idx < out_cap) {
@@ -24,7 +27,7 @@ __global__ void advance_kernel(const int64_t* __restrict__ next, const float* __
 
 void launch_advance(const int64_t* next, const float* gap, int64_t* out, float* gaps_out, int64_t out_cap,
                     int32_t* seq_pos, int32_t* counter, int64_t batch, int32_t set_pos, cudaStream_t s) {
-    advance_kernel<<<1, 256, 0, s>>>(next, gap, out, gaps_out, out_cap, seq_pos, counter, batch, set_pos);
+    launch_pdl(advance_kernel, dim3(1), dim3(256), 0, s, next, gap, out, gaps_out, out_cap, seq_pos, counter, batch, set_pos);
 }
 
 }  // namespace amcu

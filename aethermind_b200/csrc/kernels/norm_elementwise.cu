@@ -16,6 +16,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ in, 
                                                       T* __restrict__ out, const T* __restrict__ res,
                                                       T* res_out, int64_t hidden, int64_t in_stride,
                                                       int64_t out_stride, float eps) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;
     const T* x = in + row * in_stride;
     const T* r = res ? res + row * in_stride : nullptr;
@@ -50,12 +52,16 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ in, 
 
 template <typename T>
 __global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ o, int64_t n) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         o[i] = Act<T>::store(Act<T>::load(a[i]) + Act<T>::load(b[i]));
 }
 
 template <typename T>
 __global__ void silu_mul_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ o, int64_t n) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         o[i] = Act<T>::store(silu_ref(Act<T>::load(g[i])) * Act<T>::load(u[i]));
 }
@@ -67,6 +73,8 @@ template <typename T, typename Id>
 __global__ void embedding_kernel(const Id* __restrict__ ids, const void* __restrict__ table,
                                  const float* __restrict__ row_scales, int64_t vocab, int64_t hidden,
                                  T* __restrict__ out, int32_t* status) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;
     const int64_t id = (int64_t)ids[row];
     T* o = out + row * hidden;
@@ -109,6 +117,8 @@ __device__ __forceinline__ Top2 merge_top2(Top2 a, Top2 b) {
 template <typename T>
 __global__ void __launch_bounds__(1024) argmax_kernel(const T* __restrict__ logits, int64_t vocab, int64_t stride,
                                                       int64_t* __restrict__ out_idx, float* __restrict__ out_gap) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;
     const T* l = logits + row * stride;
     Top2 t{-INFINITY, INT64_MAX, -INFINITY};
@@ -142,6 +152,8 @@ constexpr int kArgmaxParts = 64;
 template <typename T>
 __global__ void __launch_bounds__(256) argmax_partial_kernel(const T* __restrict__ logits, int64_t vocab,
                                                              int64_t stride, Top2* __restrict__ parts) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.y;
     const T* l = logits + row * stride;
     constexpr int V = 16 / sizeof(T);
@@ -186,6 +198,8 @@ __global__ void __launch_bounds__(256) argmax_partial_kernel(const T* __restrict
 
 __global__ void argmax_final_kernel(const Top2* __restrict__ parts, int nparts, int64_t* __restrict__ out_idx,
                                     float* __restrict__ out_gap) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;
     Top2 t{-INFINITY, INT64_MAX, -INFINITY};
     for (int i = threadIdx.x; i < nparts; i += blockDim.x) t = merge_top2(t, parts[row * nparts + i]);
@@ -308,11 +322,11 @@ am_status_code amcu_rmsnorm(const AmcuRmsNormArgs* a, void* stream) {
     AMCU_REQUIRE(is >= a->hidden && os >= a->hidden, "amcu_rmsnorm: row stride smaller than hidden");
     const int threads = a->hidden >= 1024 ? 256 : 128;
     if (a->dtype == AMCU_F32)
-        rmsnorm_kernel<float><<<(unsigned)a->rows, threads, 0, as_stream(stream)>>>(
+        launch_pdl(rmsnorm_kernel<float>, dim3((unsigned)a->rows), dim3(threads), 0, as_stream(stream), 
                 (const float*)a->input, (const float*)a->weight, (float*)a->output, (const float*)a->residual,
                 (float*)a->residual_out, a->hidden, is, os, a->eps);
     else
-        rmsnorm_kernel<__nv_bfloat16><<<(unsigned)a->rows, threads, 0, as_stream(stream)>>>(
+        launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3((unsigned)a->rows), dim3(threads), 0, as_stream(stream), 
                 (const __nv_bfloat16*)a->input, (const __nv_bfloat16*)a->weight, (__nv_bfloat16*)a->output,
                 (const __nv_bfloat16*)a->residual, (__nv_bfloat16*)a->residual_out, a->hidden, is, os, a->eps);
     return check_launch("amcu_rmsnorm");
@@ -325,10 +339,10 @@ am_status_code amcu_add(const void* x, const void* y, void* out, int64_t n, int3
     AMCU_REQUIRE(x && y && out, "amcu_add: null pointer");
     AMCU_REQUIRE(dtype == AMCU_F32 || dtype == AMCU_BF16, "amcu_add: dtype must be f32 or bf16");
     if (dtype == AMCU_F32)
-        add_kernel<float><<<grid_for(n, 256), 256, 0, as_stream(stream)>>>((const float*)x, (const float*)y,
+        launch_pdl(add_kernel<float>, dim3(grid_for(n, 256)), dim3(256), 0, as_stream(stream), (const float*)x, (const float*)y,
                                                                           (float*)out, n);
     else
-        add_kernel<__nv_bfloat16><<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(
+        launch_pdl(add_kernel<__nv_bfloat16>, dim3(grid_for(n, 256)), dim3(256), 0, as_stream(stream), 
                 (const __nv_bfloat16*)x, (const __nv_bfloat16*)y, (__nv_bfloat16*)out, n);
     return check_launch("amcu_add");
 }
@@ -340,10 +354,10 @@ am_status_code amcu_silu_mul(const void* g, const void* u, void* out, int64_t n,
     AMCU_REQUIRE(g && u && out, "amcu_silu_mul: null pointer");
     AMCU_REQUIRE(dtype == AMCU_F32 || dtype == AMCU_BF16, "amcu_silu_mul: dtype must be f32 or bf16");
     if (dtype == AMCU_F32)
-        silu_mul_kernel<float><<<grid_for(n, 256), 256, 0, as_stream(stream)>>>((const float*)g, (const float*)u,
+        launch_pdl(silu_mul_kernel<float>, dim3(grid_for(n, 256)), dim3(256), 0, as_stream(stream), (const float*)g, (const float*)u,
                                                                                (float*)out, n);
     else
-        silu_mul_kernel<__nv_bfloat16><<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(
+        launch_pdl(silu_mul_kernel<__nv_bfloat16>, dim3(grid_for(n, 256)), dim3(256), 0, as_stream(stream), 
                 (const __nv_bfloat16*)g, (const __nv_bfloat16*)u, (__nv_bfloat16*)out, n);
     return check_launch("amcu_silu_mul");
 }
@@ -360,7 +374,7 @@ am_status_code amcu_embedding(const AmcuEmbeddingArgs* a, void* stream) {
     const dim3 grid((unsigned)a->count);
     cudaStream_t s = as_stream(stream);
 #define AMCU_EMB(T, ID) \
-    embedding_kernel<T, ID><<<grid, 256, 0, s>>>((const ID*)a->ids, a->table, a->row_scales, a->vocab, a->hidden, (T*)a->out, a->status)
+    launch_pdl(embedding_kernel<T, ID>, grid, dim3(256), 0, s, (const ID*)a->ids, a->table, a->row_scales, a->vocab, a->hidden, (T*)a->out, a->status)
     if (a->dtype == AMCU_F32) {
         if (a->id_dtype == AMCU_I32) AMCU_EMB(float, int32_t);
         else if (a->id_dtype == AMCU_I64) AMCU_EMB(float, int64_t);
@@ -383,10 +397,10 @@ am_status_code amcu_argmax(const void* logits, int64_t rows, int64_t vocab, int6
     if (stride == 0) stride = vocab;
     AMCU_REQUIRE(stride >= vocab, "amcu_argmax: row stride smaller than vocab");
     if (dtype == AMCU_F32)
-        argmax_kernel<float><<<(unsigned)rows, 1024, 0, as_stream(stream)>>>((const float*)logits, vocab, stride,
+        launch_pdl(argmax_kernel<float>, dim3((unsigned)rows), dim3(1024), 0, as_stream(stream), (const float*)logits, vocab, stride,
                                                                              out_idx, out_gap);
     else if (dtype == AMCU_BF16)
-        argmax_kernel<__nv_bfloat16><<<(unsigned)rows, 1024, 0, as_stream(stream)>>>(
+        launch_pdl(argmax_kernel<__nv_bfloat16>, dim3((unsigned)rows), dim3(1024), 0, as_stream(stream), 
                 (const __nv_bfloat16*)logits, vocab, stride, out_idx, out_gap);
     else
         return set_error(AM_STATUS_INVALID_ARGUMENT, "amcu_argmax: dtype must be f32 or bf16");
@@ -411,13 +425,13 @@ am_status_code amcu_argmax_ws(const void* logits, int64_t rows, int64_t vocab, i
     const dim3 grid(kArgmaxParts, (unsigned)rows);
     Top2* parts = static_cast<Top2*>(workspace);
     if (dtype == AMCU_F32)
-        argmax_partial_kernel<float><<<grid, 256, 0, as_stream(stream)>>>((const float*)logits, vocab, stride, parts);
+        launch_pdl(argmax_partial_kernel<float>, grid, dim3(256), 0, as_stream(stream), (const float*)logits, vocab, stride, parts);
     else if (dtype == AMCU_BF16)
-        argmax_partial_kernel<__nv_bfloat16><<<grid, 256, 0, as_stream(stream)>>>((const __nv_bfloat16*)logits, vocab,
+        launch_pdl(argmax_partial_kernel<__nv_bfloat16>, grid, dim3(256), 0, as_stream(stream), (const __nv_bfloat16*)logits, vocab,
                                                                                   stride, parts);
     else
         return set_error(AM_STATUS_INVALID_ARGUMENT, "amcu_argmax_ws: dtype must be f32 or bf16");
-    argmax_final_kernel<<<(unsigned)rows, 32, 0, as_stream(stream)>>>(parts, kArgmaxParts, out_idx, out_gap);
+    launch_pdl(argmax_final_kernel, dim3((unsigned)rows), dim3(32), 0, as_stream(stream), parts, kArgmaxParts, out_idx, out_gap);
     return check_launch("amcu_argmax_ws");
 }
 

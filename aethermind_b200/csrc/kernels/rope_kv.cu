@@ -35,6 +35,8 @@ __global__ void rope_table_kernel(double theta, int64_t d, int64_t max_pos, floa
 // heads (copied into the cache). Thread i handles the pair (i, i + d/2).
 template <typename T>
 __global__ void __launch_bounds__(64) rope_kv_kernel(AmcuRopeKvArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t row = blockIdx.x;
     const int64_t head = blockIdx.y;
     const int64_t b = row / a.rows_per_seq;
@@ -93,9 +95,9 @@ extern "C" am_status_code amcu_rope_kv_write(const AmcuRopeKvArgs* a, void* stre
     AMCU_REQUIRE(a->theta > 0.0, "amcu_rope_kv_write: theta must be positive");
     const dim3 grid((unsigned)a->rows, (unsigned)(a->n_q_heads + 2 * a->n_kv_heads));
     if (a->dtype == AMCU_F32)
-        rope_kv_kernel<float><<<grid, 64, 0, as_stream(stream)>>>(*a);
+        launch_pdl(rope_kv_kernel<float>, grid, dim3(64), 0, as_stream(stream), *a);
     else if (a->dtype == AMCU_BF16)
-        rope_kv_kernel<__nv_bfloat16><<<grid, 64, 0, as_stream(stream)>>>(*a);
+        launch_pdl(rope_kv_kernel<__nv_bfloat16>, grid, dim3(64), 0, as_stream(stream), *a);
     else
         return set_error(AM_STATUS_INVALID_ARGUMENT, "amcu_rope_kv_write: dtype must be f32 or bf16");
     return check_launch("amcu_rope_kv_write");

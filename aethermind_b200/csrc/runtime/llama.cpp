@@ -173,10 +173,9 @@ Status SliceCanon(am_model_s* m, const Canon& src, int64_t r0, int64_t nr, int64
 // Prepacks a canonical matrix into rows [row0, row0 + n) of a device weight.
 Status PackInto(am_model_s* m, LinearWeight& lw, int64_t row0, const Canon& cn) {
     const auto& c = m->cfg;
-    char* qd = static_cast<char*>(lw.q.data()) + row0 * RowBytes(c, lw.w.k);
-    char* sd = lw.s.data() ? static_cast<char*>(lw.s.data()) + row0 * ScaleRowBytes(c, lw.w.k) : nullptr;
-    am_status_code st = amcu_prepack_weight(c.weight_format, c.act_dtype, cn.n, cn.k, c.group_size, cn.q.data(),
-                                            cn.s.data(), qd, sd, m->rt->stream);
+    am_status_code st = amcu_prepack_weight_rows(c.weight_format, c.act_dtype, cn.n, cn.k, c.group_size, lw.w.n,
+                                                 row0, cn.q.data(), cn.s.data(), lw.q.data(), lw.s.data(),
+                                                 m->rt->stream);
     AM_RETURN_IF_ERROR(Status::FromAm(st, amcu_last_error()));
     // The canonical staging buffers are freed by the caller right after this;
     // the copy on the engine's non-blocking stream must have read them first.

@@ -124,6 +124,14 @@ int64_t amcu_packed_scale_bytes(int32_t format, int64_t n, int64_t k, int64_t gr
 am_status_code amcu_prepack_weight(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group,
                                    const void* q_canonical, const void* s_canonical,
                                    void* q_packed, void* s_packed, void* stream);
+/* canonical [n][k] part -> rows [row0, row0 + n) of a packed [n_total][k]
+ * device weight (q_packed / s_packed point at the whole packed weight; row0 a
+ * multiple of 16). Builds a fused weight (e.g. Q, K and V projections in one
+ * [nq+2nkv][k] matrix) part by part, as the reference's loader fills one
+ * fused tensor from several checkpoint tensors. */
+am_status_code amcu_prepack_weight_rows(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group,
+                                        int64_t n_total, int64_t row0, const void* q_canonical,
+                                        const void* s_canonical, void* q_packed, void* s_packed, void* stream);
 /* device format -> canonical (for round-trip checks and checkpoint export). */
 am_status_code amcu_unpack_weight(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group,
                                   const void* q_packed, const void* s_packed,

@@ -61,9 +61,10 @@ def test_synth_bit_exact_vs_oracle(ops, orc):
 
 
 @pytest.mark.parametrize("fmt", ["int4", "int8"])
-def test_prepack_roundtrip_bit_exact(ops, fmt):
+@pytest.mark.parametrize("k", [1024, 384, 1792])  # 8 chunks; 2 chunks with padding tiles; 7 chunks
+def test_prepack_roundtrip_bit_exact(ops, fmt, k):
     from aethermind_b200 import _lib as L
-    n, k = 96, 1024
+    n = 96
     if fmt == "int4":
         q, s = ops.synth_w4(3, 1, n, k, 0.01)
         pw = ops.prepack(L.WFMT_INT4, q, s, n, k)
@@ -73,6 +74,35 @@ def test_prepack_roundtrip_bit_exact(ops, fmt):
     q2, s2 = ops.unpack(pw)
     assert torch.equal(q2.view(torch.uint8).flatten(), q.view(torch.uint8).flatten())
     assert torch.equal(s2.flatten().view(torch.uint8), s.flatten().view(torch.uint8))
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
+def test_prepack_rows_builds_fused_weight(ops, fmt):
+    """Packing row ranges one by one into a fused weight gives the same bytes
+    as packing the concatenated canonical matrix (the q/k/v fusion)."""
+    import ctypes as C
+    from aethermind_b200 import _lib as L
+    k, parts = 1792, [64, 32, 32]
+    f = L.WFMT_INT4 if fmt == "int4" else L.WFMT_INT8
+    syn = ops.synth_w4 if fmt == "int4" else ops.synth_w8
+    qs, ss = zip(*[syn(7, i, n, k, 0.01) for i, n in enumerate(parts)])
+    n_total = sum(parts)
+    whole = ops.prepack(f, torch.cat(qs), torch.cat(ss), n_total, k)
+    fused = ops.prepack(f, torch.cat(qs), torch.cat(ss), n_total, k)
+    fused.data.zero_()
+    fused.scales.zero_()
+    row0 = 0
+    for q, s, n in zip(qs, ss, parts):
+        code = L.lib().amcu_prepack_weight_rows(f, L.BF16, n, k, 128, n_total, row0, q.data_ptr(), s.data_ptr(),
+                                                fused.data.data_ptr(), fused.scales.data_ptr(),
+                                                torch.cuda.current_stream().cuda_stream)
+        L.check(code, "amcu_prepack_weight_rows")
+        row0 += n
+    torch.cuda.synchronize()
+    assert torch.equal(fused.data, whole.data) and torch.equal(fused.scales, whole.scales)
+    bad = L.lib().amcu_prepack_weight_rows(f, L.BF16, 32, k, 128, n_total, 8, qs[1].data_ptr(), ss[1].data_ptr(),
+                                           fused.data.data_ptr(), fused.scales.data_ptr(), None)
+    assert bad == 3 and b"16-row" in L.lib().amcu_last_error()
 
 
 # ------------------------------------------------------------- rmsnorm
@@ -126,6 +156,19 @@ def test_gemv_matches_oracle(ops, orc, fmt, m, n):
     x = orc.bf16_round(np.random.default_rng(m).normal(0, 1, (m, k)).astype(np.float32))
     entry = "amcu_gemv_w4g128" if fmt == "int4" else "amcu_gemv_w8"
     y = ops.linear(bf16_dev(x), pw, entry=entry)
+    np.testing.assert_allclose(to_np(y), _oracle_linear(orc, fmt, x, host), rtol=BF_RTOL, atol=BF_ATOL)
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
+@pytest.mark.parametrize("m", [1, 3])
+@pytest.mark.parametrize("k", [384, 1792, 14336])
+def test_gemv_stream_geometries(ops, orc, fmt, m, k):
+    """K values whose stream layout pads tiles (384), uses 7 chunks (1792) or
+    long chunks (14336)."""
+    n = 48
+    pw, host = _w(ops, orc, fmt, n, k, seed=k)
+    x = orc.bf16_round(np.random.default_rng(k + m).normal(0, 1, (m, k)).astype(np.float32))
+    y = ops.linear(bf16_dev(x), pw)
     np.testing.assert_allclose(to_np(y), _oracle_linear(orc, fmt, x, host), rtol=BF_RTOL, atol=BF_ATOL)
 
 

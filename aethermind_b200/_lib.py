@@ -46,11 +46,16 @@ class AmcuRmsNormArgs(C.Structure):
                 ("eps", C.c_float), ("dtype", C.c_int32)]
 
 
+class AmcuL2Prefetch(C.Structure):
+    _fields_ = [("ptr", C.c_void_p * 4), ("bytes", C.c_uint64 * 4)]
+
+
 class AmcuLinearArgs(C.Structure):
     _fields_ = [("x", C.c_void_p), ("w", AmcuWeight), ("y", C.c_void_p), ("residual", C.c_void_p),
                 ("m", C.c_int64), ("x_stride", C.c_int64), ("y_stride", C.c_int64),
                 ("act_dtype", C.c_int32), ("epilogue", C.c_int32), ("workspace", C.c_void_p),
-                ("workspace_size", C.c_size_t), ("norm_weight", C.c_void_p), ("norm_eps", C.c_float)]
+                ("workspace_size", C.c_size_t), ("norm_weight", C.c_void_p), ("norm_eps", C.c_float),
+                ("l2_next", AmcuL2Prefetch)]
 
 
 class AmcuRopeKvArgs(C.Structure):
@@ -91,7 +96,7 @@ class AmModelConfig(C.Structure):
 
 
 class AmSessionConfig(C.Structure):
-    _fields_ = [("max_new_tokens", C.c_int64), ("use_cuda_graph", C.c_int32)]
+    _fields_ = [("max_new_tokens", C.c_int64), ("use_cuda_graph", C.c_int32), ("unfused_attention", C.c_int32)]
 
 
 P = C.c_void_p
@@ -126,6 +131,7 @@ _SIGS = {
     "amcu_attn_decode": (C.c_int, [C.POINTER(AmcuAttentionArgs), P]),
     "amcu_attn_prefill": (C.c_int, [C.POINTER(AmcuAttentionArgs), P]),
     "amcu_attn_decode_noalloc": (C.c_int, [C.POINTER(AmcuAttentionArgs), P]),
+    "amcu_attn_decode_rope": (C.c_int, [C.POINTER(AmcuRopeKvArgs), C.POINTER(AmcuAttentionArgs), P]),
     "amcu_silu_mul": (C.c_int, [P, P, P, C.c_int64, C.c_int32, P]),
     "amcu_add": (C.c_int, [P, P, P, C.c_int64, C.c_int32, P]),
     "amcu_argmax": (C.c_int, [P, C.c_int64, C.c_int64, C.c_int64, C.c_int32, P, P, P]),

@@ -15,12 +15,10 @@
 #include <mutex>
 
 #include "../amcu_internal.h"
+#include "attn_decode.cuh"
 #include "common.cuh"
 
 namespace amcu {
-
-constexpr int kAttnThreads = 128;
-constexpr float kLog2e = 1.4426950408889634f;
 
 template <typename T>
 __device__ __forceinline__ void load8(const T* p, float (&f)[8]);
@@ -181,22 +179,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_splitk_kernel(AttnKParams p
 
 
 // Decode kernel (one query row per sequence, long context): the same split /
-// combine structure, with a warp scoring 8 keys at a time. Lane 4k+q holds
-// quarter q of key k's head_dim: four 16-byte K loads per lane, a two-shuffle
-// reduction, one online-softmax update per 8-key block, then P*V with lane l
-// owning head_dim/32 output dims of every head (V rows read coalesced).
+// combine structure, with a warp scoring 8 keys at a time (decode_keys_warp).
 template <typename T, int GRP, int D>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnKParams p) {
     pdl_wait();
     pdl_trigger();
-    constexpr int NW = kAttnThreads / 32;
-    constexpr int DQ = D / 4;   // dims per lane in the QK phase
-    constexpr int DL = D / 32;  // dims per lane in the PV phase
     static_assert(sizeof(T) == 2, "bf16 only");
     const int split = blockIdx.x, kvh = blockIdx.y;
     const int64_t row = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kk = lane >> 2, qd = lane & 3;
     const int64_t b = row / p.rows_per_seq;
     const int64_t pos = (int64_t)p.seq_pos[b] + row % p.rows_per_seq;
     const int64_t L = pos + 1;
@@ -206,122 +197,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnKParams p
     const int64_t k_end = k_begin + chunk < L ? k_begin + chunk : L;
 
     __shared__ __align__(16) float qs[GRP][D];
-    __shared__ float sm_m[NW][GRP], sm_l[NW][GRP];
-    __shared__ float sm_o[NW][GRP][D];
+    __shared__ float sm_m[kAttnWarps][GRP], sm_l[kAttnWarps][GRP];
+    __shared__ float sm_o[kAttnWarps][GRP][D];
     const T* qrow = static_cast<const T*>(p.q) + row * p.q_stride + (int64_t)kvh * GRP * D;
     for (int i = threadIdx.x; i < GRP * D; i += kAttnThreads) qs[i / D][i % D] = Act<T>::load(qrow[i]) * p.scale_log2;
     __syncthreads();
 
     const T* kbase = static_cast<const T*>(p.kc) + b * p.slot_stride + (int64_t)kvh * p.capacity * D;
     const T* vbase = static_cast<const T*>(p.vc) + b * p.slot_stride + (int64_t)kvh * p.capacity * D;
-
-    float m[GRP], l[GRP], acc[GRP][DL];
-#pragma unroll
-    for (int h = 0; h < GRP; ++h) {
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-#pragma unroll
-        for (int i = 0; i < DL; ++i) acc[h][i] = 0.f;
-    }
-
-    for (int64_t kb = k_begin + warp * 8; kb < k_end; kb += NW * 8) {
-        const int64_t key = kb + kk;
-        const bool valid = key < k_end;
-        // K quarter of this lane's key, V slices of the block's 8 keys
-        uint4 kv4[DQ / 8];
-#pragma unroll
-        for (int i = 0; i < DQ / 8; ++i)
-            kv4[i] = valid ? *reinterpret_cast<const uint4*>(kbase + key * D + qd * DQ + i * 8) : make_uint4(0, 0, 0, 0);
-        const int nk = (int)(k_end - kb < 8 ? k_end - kb : 8);
-        float vf[8][DL];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            if (j < nk) {
-                const T* vr = vbase + (kb + j) * D + lane * DL;
-                if constexpr (DL == 4) {
-                    const uint2 u = *reinterpret_cast<const uint2*>(vr);
-                    vf[j][0] = __uint_as_float(u.x << 16); vf[j][1] = __uint_as_float(u.x & 0xffff0000u);
-                    vf[j][2] = __uint_as_float(u.y << 16); vf[j][3] = __uint_as_float(u.y & 0xffff0000u);
-                } else {
-                    const uint32_t u = *reinterpret_cast<const uint32_t*>(vr);
-                    vf[j][0] = __uint_as_float(u << 16); vf[j][1] = __uint_as_float(u & 0xffff0000u);
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < DL; ++i) vf[j][i] = 0.f;
-            }
-        }
-        float s[GRP];
-#pragma unroll
-        for (int h = 0; h < GRP; ++h) s[h] = 0.f;
-#pragma unroll
-        for (int i = 0; i < DQ / 8; ++i) {
-            const uint32_t w4[4] = {kv4[i].x, kv4[i].y, kv4[i].z, kv4[i].w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float k0 = __uint_as_float(w4[e] << 16), k1 = __uint_as_float(w4[e] & 0xffff0000u);
-                const int dd = qd * DQ + i * 8 + 2 * e;
-#pragma unroll
-                for (int h = 0; h < GRP; ++h) {
-                    const float2 qq = *reinterpret_cast<const float2*>(&qs[h][dd]);
-                    s[h] = fmaf(qq.x, k0, fmaf(qq.y, k1, s[h]));
-                }
-            }
-        }
-        float pr[GRP];
-#pragma unroll
-        for (int h = 0; h < GRP; ++h) {
-            s[h] += __shfl_xor_sync(0xffffffffu, s[h], 1);
-            s[h] += __shfl_xor_sync(0xffffffffu, s[h], 2);
-            const float sv = valid ? s[h] : -INFINITY;
-            float bm = fmaxf(sv, __shfl_xor_sync(0xffffffffu, sv, 4));
-            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
-            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
-            const float mn = fmaxf(m[h], bm);
-            const float corr = exp2f(m[h] - mn);
-            pr[h] = valid ? exp2f(sv - mn) : 0.f;
-            float bs = pr[h] + __shfl_xor_sync(0xffffffffu, pr[h], 4);
-            bs += __shfl_xor_sync(0xffffffffu, bs, 8);
-            bs += __shfl_xor_sync(0xffffffffu, bs, 16);
-            l[h] = l[h] * corr + bs;
-            m[h] = mn;
-#pragma unroll
-            for (int i = 0; i < DL; ++i) acc[h][i] *= corr;
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-#pragma unroll
-            for (int h = 0; h < GRP; ++h) {
-                const float pj = __shfl_sync(0xffffffffu, pr[h], 4 * j);
-#pragma unroll
-                for (int i = 0; i < DL; ++i) acc[h][i] = fmaf(pj, vf[j][i], acc[h][i]);
-            }
-        }
-    }
-
-    if (lane == 0) {
-#pragma unroll
-        for (int h = 0; h < GRP; ++h) { sm_m[warp][h] = m[h]; sm_l[warp][h] = l[h]; }
-    }
-#pragma unroll
-    for (int h = 0; h < GRP; ++h)
-#pragma unroll
-        for (int i = 0; i < DL; ++i) sm_o[warp][h][lane * DL + i] = acc[h][i];
+    DecodeWarpState<GRP, D> st;
+    decode_keys_warp<GRP, D>(kbase, vbase, k_begin, k_end, warp, lane, qs, st);
+    decode_publish_warp<GRP, D>(st, warp, lane, sm_m, sm_l, sm_o);
     __syncthreads();
     for (int e = threadIdx.x; e < GRP * D; e += kAttnThreads) {
         const int h = e / D, dd = e % D;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w][h]);
-        float Ls = 0.f, O = 0.f;
-        if (M != -INFINITY) {
-#pragma unroll
-            for (int w = 0; w < NW; ++w) {
-                const float f = exp2f(sm_m[w][h] - M);
-                Ls += sm_l[w][h] * f;
-                O += sm_o[w][h][dd] * f;
-            }
-        }
+        float M, Ls, O;
+        decode_merge_warps<GRP, D>(h, dd, sm_m, sm_l, sm_o, M, Ls, O);
         const int64_t qh = (int64_t)kvh * GRP + h;
         if (p.nsplit == 1) {
             T* o = static_cast<T*>(p.out) + row * p.out_stride + qh * D;

@@ -1,0 +1,258 @@
+// Fused decode step of the attention block: RoPE of q and k, the KV-cache
+// append of this token, split-K attention over the cache and the merge of the
+// splits, in one launch.
+//
+// Semantics: exactly amcu_rope_kv_write followed by amcu_attn_decode (the
+// reference's RoPE, KVCacheUpdate and Attention nodes,
+// src/operators/rope_op.cpp:202-223, src/operators/kvcache_update_op.cpp:142-158,
+// src/operators/attention_op.cpp:151-169), except that the rotated q is not
+// written back: it is rounded to bf16 as the in-place store would round it
+// and used on chip.
+//
+// Layout of the work: one thread-block cluster per (sequence, kv head), its
+// CTAs splitting the sequence [0, pos] into equal chunks of whole 8-key
+// blocks. Every CTA rotates the GRP query heads itself; the CTA whose chunk
+// holds `pos` also rotates k and appends k and v to the cache before reading
+// its chunk. Each CTA merges its warps into a (max, sum, unnormalised output)
+// partial in shared memory; after a cluster barrier every CTA combines a
+// slice of the outputs by reading all partials through distributed shared
+// memory, and a second barrier keeps the partials alive until all reads are
+// done. No workspace, no second kernel.
+#include <cooperative_groups.h>
+
+#include "../amcu_internal.h"
+#include "attn_decode.cuh"
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace amcu {
+
+struct RopeAttnParams {
+    const __nv_bfloat16 *q, *k, *v;
+    int64_t q_stride, k_stride, v_stride;
+    __nv_bfloat16 *kc, *vc;
+    int64_t slot_stride, capacity;
+    const int32_t* seq_pos;
+    int32_t* status;
+    const float* cos_sin;
+    double theta;
+    __nv_bfloat16* out;
+    int64_t out_stride;
+    float scale_log2;
+};
+
+template <int GRP, int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(RopeAttnParams p) {
+    pdl_wait();
+    pdl_trigger();
+    constexpr int HALF = D / 2;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
+    const int kvh = blockIdx.y;
+    const int64_t row = blockIdx.z;  // one row per sequence
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t pos = p.seq_pos[row];
+    if (pos < 0 || pos >= p.capacity) {  // the whole cluster leaves together
+        if (rank == 0 && kvh == 0 && threadIdx.x == 0 && p.status) atomicExch(p.status, (int32_t)AM_STATUS_OUT_OF_RANGE);
+        return;
+    }
+    const int64_t L = pos + 1;
+    int64_t chunk = (L + cs - 1) / cs;
+    chunk = (chunk + 7) / 8 * 8;
+    const int64_t k_begin = (int64_t)rank * chunk;
+    const int64_t k_end = k_begin + chunk < L ? k_begin + chunk : L;
+
+    __shared__ __align__(16) float qs[GRP][D];
+    __shared__ float sm_m[kAttnWarps][GRP], sm_l[kAttnWarps][GRP];
+    __shared__ float sm_o[kAttnWarps][GRP][D];
+    __shared__ float pm[GRP], pl[GRP];
+    __shared__ float po[GRP][D];
+
+    auto angle = [&](int i, float& c, float& s) {
+        if (p.cos_sin) {
+            const float2 v = reinterpret_cast<const float2*>(p.cos_sin)[pos * HALF + i];
+            c = v.x;
+            s = v.y;
+        } else {
+            rope_angle(p.theta, D, pos, i, c, s);
+        }
+    };
+    // query heads kvh*GRP .. kvh*GRP + GRP - 1, rotated and rounded to bf16
+    const __nv_bfloat16* qrow = p.q + row * p.q_stride + (int64_t)kvh * GRP * D;
+    for (int i = threadIdx.x; i < GRP * HALF; i += kAttnThreads) {
+        const int h = i / HALF, j = i % HALF;
+        float c, s;
+        angle(j, c, s);
+        const float x1 = __bfloat162float(qrow[h * D + j]), x2 = __bfloat162float(qrow[h * D + j + HALF]);
+        const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        const float o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+        qs[h][j] = Act<__nv_bfloat16>::round(o1) * p.scale_log2;
+        qs[h][j + HALF] = Act<__nv_bfloat16>::round(o2) * p.scale_log2;
+    }
+    __nv_bfloat16* kbase = p.kc + row * p.slot_stride + (int64_t)kvh * p.capacity * D;
+    __nv_bfloat16* vbase = p.vc + row * p.slot_stride + (int64_t)kvh * p.capacity * D;
+    if (k_begin <= pos && pos < k_end) {  // this CTA's chunk holds the new token: append it
+        const __nv_bfloat16* krow = p.k + row * p.k_stride + (int64_t)kvh * D;
+        const __nv_bfloat16* vrow = p.v + row * p.v_stride + (int64_t)kvh * D;
+        for (int j = threadIdx.x; j < HALF; j += kAttnThreads) {
+            float c, s;
+            angle(j, c, s);
+            const float x1 = __bfloat162float(krow[j]), x2 = __bfloat162float(krow[j + HALF]);
+            kbase[pos * D + j] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
+            kbase[pos * D + j + HALF] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
+        }
+        for (int j = threadIdx.x; j < D; j += kAttnThreads) vbase[pos * D + j] = vrow[j];
+    }
+    __syncthreads();  // q staged; the appended row is visible to this CTA's reads
+
+    DecodeWarpState<GRP, D> st;
+    decode_keys_warp<GRP, D>(kbase, vbase, k_begin, k_end, warp, lane, qs, st);
+    decode_publish_warp<GRP, D>(st, warp, lane, sm_m, sm_l, sm_o);
+    __syncthreads();
+    for (int e = threadIdx.x; e < GRP * D; e += kAttnThreads) {
+        const int h = e / D, dd = e % D;
+        float M, Ls, O;
+        decode_merge_warps<GRP, D>(h, dd, sm_m, sm_l, sm_o, M, Ls, O);
+        po[h][dd] = O;
+        if (dd == 0) {
+            pm[h] = M;
+            pl[h] = Ls;
+        }
+    }
+    cluster.sync();  // every CTA's partial is complete
+
+    for (int e = rank * kAttnThreads + threadIdx.x; e < GRP * D; e += cs * kAttnThreads) {
+        const int h = e / D, dd = e % D;
+        float M = -INFINITY;
+        for (int r = 0; r < cs; ++r) M = fmaxf(M, cluster.map_shared_rank(pm, r)[h]);
+        float Ls = 0.f, O = 0.f;
+        for (int r = 0; r < cs; ++r) {
+            const float m = cluster.map_shared_rank(pm, r)[h];
+            if (m == -INFINITY) continue;  // an empty chunk
+            const float f = exp2f(m - M);
+            Ls += cluster.map_shared_rank(pl, r)[h] * f;
+            O += cluster.map_shared_rank(&po[0][0], r)[h * D + dd] * f;
+        }
+        p.out[row * p.out_stride + ((int64_t)kvh * GRP + h) * D + dd] = __float2bfloat16_rn(O / Ls);
+    }
+    cluster.sync();  // partials stay alive until every CTA has read them
+}
+
+template <int GRP, int D>
+static cudaError_t launch_rope_attn(const RopeAttnParams& p, int cs, int64_t nkv, int64_t rows, cudaStream_t s) {
+    auto kern = attn_rope_decode_kernel<GRP, D>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        attr_set = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)cs, (unsigned)nkv, (unsigned)rows);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+// Cluster size: 16 CTAs per (sequence, kv head) where the device schedules
+// clusters that large, else the portable 8.
+template <int GRP, int D>
+static int cluster_size() {
+    static int cs = 0;
+    if (cs == 0) {
+        auto kern = attn_rope_decode_kernel<GRP, D>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(16, 1, 1);
+        cfg.blockDim = dim3(kAttnThreads);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 16;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+        if (e != cudaSuccess) cudaGetLastError();
+        cs = (e == cudaSuccess && n > 0) ? 16 : 8;
+    }
+    return cs;
+}
+
+template <int D>
+static bool dispatch_rope_attn(const RopeAttnParams& p, int grp, int64_t nkv, int64_t rows, cudaStream_t s) {
+    switch (grp) {
+#define AMCU_RA(G)                                                                   \
+    case G: {                                                                        \
+        const cudaError_t e = launch_rope_attn<G, D>(p, cluster_size<G, D>(), nkv, rows, s); \
+        (void)e;                                                                     \
+        return true;                                                                 \
+    }
+        AMCU_RA(1)
+        AMCU_RA(2)
+        AMCU_RA(4)
+        AMCU_RA(8)
+#undef AMCU_RA
+        default: return false;
+    }
+}
+
+}  // namespace amcu
+
+using namespace amcu;
+
+extern "C" am_status_code amcu_attn_decode_rope(const AmcuRopeKvArgs* r, const AmcuAttentionArgs* a, void* stream) {
+    clear_error();
+    AMCU_REQUIRE(r && a, "amcu_attn_decode_rope: null args");
+    AMCU_REQUIRE(r->rows == a->rows && r->rows >= 0, "amcu_attn_decode_rope: rope and attention rows differ");
+    if (a->rows == 0) return AM_STATUS_OK;
+    AMCU_REQUIRE(r->rows_per_seq == 1 && a->rows_per_seq == 1, "amcu_attn_decode_rope: decode takes one row per sequence");
+    AMCU_REQUIRE(r->dtype == AMCU_BF16 && a->dtype == AMCU_BF16, "amcu_attn_decode_rope: bf16 only");
+    AMCU_REQUIRE(r->n_q_heads == a->n_q_heads && r->n_kv_heads == a->n_kv_heads && r->head_dim == a->head_dim,
+                 "amcu_attn_decode_rope: rope and attention head shapes differ");
+    AMCU_REQUIRE(r->k_cache == a->k_cache && r->v_cache == a->v_cache && r->seq_pos == a->seq_pos &&
+                         r->capacity == a->capacity,
+                 "amcu_attn_decode_rope: rope and attention must name the same cache and positions");
+    AMCU_REQUIRE(r->q == a->q, "amcu_attn_decode_rope: attention q must be the rope q");
+    AMCU_REQUIRE(r->q && r->k && r->v && a->k_cache && a->v_cache && a->seq_pos && a->out,
+                 "amcu_attn_decode_rope: null pointer");
+    AMCU_REQUIRE(a->head_dim == 64 || a->head_dim == 128, "amcu_attn_decode_rope: head_dim must be 64 or 128");
+    AMCU_REQUIRE(a->n_kv_heads > 0 && a->n_q_heads % a->n_kv_heads == 0,
+                 "amcu_attn_decode_rope: n_q must be a multiple of n_kv");
+    AMCU_REQUIRE(a->capacity > 0 && r->theta > 0.0, "amcu_attn_decode_rope: bad capacity or theta");
+    AMCU_REQUIRE(aligned(a->k_cache, 16) && aligned(a->v_cache, 16), "amcu_attn_decode_rope: caches must be 16-byte aligned");
+    RopeAttnParams p{};
+    p.q = static_cast<const __nv_bfloat16*>(r->q);
+    p.k = static_cast<const __nv_bfloat16*>(r->k);
+    p.v = static_cast<const __nv_bfloat16*>(r->v);
+    p.q_stride = r->q_stride ? r->q_stride : r->n_q_heads * r->head_dim;
+    p.k_stride = r->k_stride ? r->k_stride : r->n_kv_heads * r->head_dim;
+    p.v_stride = r->v_stride ? r->v_stride : r->n_kv_heads * r->head_dim;
+    p.kc = static_cast<__nv_bfloat16*>(r->k_cache);
+    p.vc = static_cast<__nv_bfloat16*>(r->v_cache);
+    p.capacity = a->capacity;
+    p.slot_stride = a->slot_stride ? a->slot_stride : a->n_kv_heads * a->capacity * a->head_dim;
+    p.seq_pos = a->seq_pos;
+    p.status = r->status;
+    p.cos_sin = r->cos_sin;
+    p.theta = r->theta;
+    p.out = static_cast<__nv_bfloat16*>(a->out);
+    p.out_stride = a->out_stride ? a->out_stride : a->n_q_heads * a->head_dim;
+    p.scale_log2 = (float)(1.0 / sqrt((double)a->head_dim)) * kLog2e;
+    const int grp = (int)(a->n_q_heads / a->n_kv_heads);
+    const cudaStream_t s = as_stream(stream);
+    const bool ok = a->head_dim == 128 ? dispatch_rope_attn<128>(p, grp, a->n_kv_heads, a->rows, s)
+                                       : dispatch_rope_attn<64>(p, grp, a->n_kv_heads, a->rows, s);
+    if (!ok) return set_error(AM_STATUS_INVALID_ARGUMENT, "amcu_attn_decode_rope: GQA group %d unsupported", grp);
+    return check_launch("amcu_attn_decode_rope");
+}

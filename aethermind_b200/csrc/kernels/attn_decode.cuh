@@ -1,0 +1,155 @@
+// Decode-attention building blocks shared by the split-K kernel and the fused
+// RoPE + attention kernel: one warp scores 8 keys per step against the GRP
+// query heads of a kv head and keeps an online softmax.
+#pragma once
+#include "common.cuh"
+
+namespace amcu {
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Per-warp running softmax state: max m (log2 domain), sum l, and the
+// unnormalised output; lane l owns output dims [l * D/32, (l+1) * D/32).
+template <int GRP, int D>
+struct DecodeWarpState {
+    float m[GRP], l[GRP], acc[GRP][D / 32];
+};
+
+// Keys [k_begin, k_end) of one (row, kv head), blocks of 8 keys round-robin
+// over the CTA's warps. qs holds the GRP query heads scaled by
+// softmax_scale * log2(e). Lane 4k+q holds quarter q of key k's head_dim:
+// four 16-byte K loads per lane, a two-shuffle reduction, one online-softmax
+// update per 8-key block, then P*V with lane l owning head_dim/32 output dims
+// of every head (V rows read coalesced).
+template <int GRP, int D>
+__device__ __forceinline__ void decode_keys_warp(const __nv_bfloat16* kbase, const __nv_bfloat16* vbase,
+                                                 int64_t k_begin, int64_t k_end, int warp, int lane,
+                                                 const float (*qs)[D], DecodeWarpState<GRP, D>& st) {
+    constexpr int DQ = D / 4;   // dims per lane in the QK phase
+    constexpr int DL = D / 32;  // dims per lane in the PV phase
+    const int kk = lane >> 2, qd = lane & 3;
+#pragma unroll
+    for (int h = 0; h < GRP; ++h) {
+        st.m[h] = -INFINITY;
+        st.l[h] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DL; ++i) st.acc[h][i] = 0.f;
+    }
+    for (int64_t kb = k_begin + warp * 8; kb < k_end; kb += kAttnWarps * 8) {
+        const int64_t key = kb + kk;
+        const bool valid = key < k_end;
+        // K quarter of this lane's key, V slices of the block's 8 keys
+        uint4 kv4[DQ / 8];
+#pragma unroll
+        for (int i = 0; i < DQ / 8; ++i)
+            kv4[i] = valid ? *reinterpret_cast<const uint4*>(kbase + key * D + qd * DQ + i * 8) : make_uint4(0, 0, 0, 0);
+        const int nk = (int)(k_end - kb < 8 ? k_end - kb : 8);
+        float vf[8][DL];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (j < nk) {
+                const __nv_bfloat16* vr = vbase + (kb + j) * D + lane * DL;
+                if constexpr (DL == 4) {
+                    const uint2 u = *reinterpret_cast<const uint2*>(vr);
+                    vf[j][0] = __uint_as_float(u.x << 16); vf[j][1] = __uint_as_float(u.x & 0xffff0000u);
+                    vf[j][2] = __uint_as_float(u.y << 16); vf[j][3] = __uint_as_float(u.y & 0xffff0000u);
+                } else {
+                    const uint32_t u = *reinterpret_cast<const uint32_t*>(vr);
+                    vf[j][0] = __uint_as_float(u << 16); vf[j][1] = __uint_as_float(u & 0xffff0000u);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < DL; ++i) vf[j][i] = 0.f;
+            }
+        }
+        float s[GRP];
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) s[h] = 0.f;
+#pragma unroll
+        for (int i = 0; i < DQ / 8; ++i) {
+            const uint32_t w4[4] = {kv4[i].x, kv4[i].y, kv4[i].z, kv4[i].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float k0 = __uint_as_float(w4[e] << 16), k1 = __uint_as_float(w4[e] & 0xffff0000u);
+                const int dd = qd * DQ + i * 8 + 2 * e;
+#pragma unroll
+                for (int h = 0; h < GRP; ++h) {
+                    const float2 qq = *reinterpret_cast<const float2*>(&qs[h][dd]);
+                    s[h] = fmaf(qq.x, k0, fmaf(qq.y, k1, s[h]));
+                }
+            }
+        }
+        float pr[GRP];
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) {
+            s[h] += __shfl_xor_sync(0xffffffffu, s[h], 1);
+            s[h] += __shfl_xor_sync(0xffffffffu, s[h], 2);
+            const float sv = valid ? s[h] : -INFINITY;
+            float bm = fmaxf(sv, __shfl_xor_sync(0xffffffffu, sv, 4));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+            bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+            const float mn = fmaxf(st.m[h], bm);
+            const float corr = exp2f(st.m[h] - mn);
+            pr[h] = valid ? exp2f(sv - mn) : 0.f;
+            float bs = pr[h] + __shfl_xor_sync(0xffffffffu, pr[h], 4);
+            bs += __shfl_xor_sync(0xffffffffu, bs, 8);
+            bs += __shfl_xor_sync(0xffffffffu, bs, 16);
+            st.l[h] = st.l[h] * corr + bs;
+            st.m[h] = mn;
+#pragma unroll
+            for (int i = 0; i < DL; ++i) st.acc[h][i] *= corr;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+            for (int h = 0; h < GRP; ++h) {
+                const float pj = __shfl_sync(0xffffffffu, pr[h], 4 * j);
+#pragma unroll
+                for (int i = 0; i < DL; ++i) st.acc[h][i] = fmaf(pj, vf[j][i], st.acc[h][i]);
+            }
+        }
+    }
+}
+
+// Publishes the warp states (sm_m/sm_l per warp, sm_o per warp) for a
+// CTA-level merge.
+template <int GRP, int D>
+__device__ __forceinline__ void decode_publish_warp(const DecodeWarpState<GRP, D>& st, int warp, int lane,
+                                                    float (*sm_m)[GRP], float (*sm_l)[GRP], float (*sm_o)[GRP][D]) {
+    constexpr int DL = D / 32;
+    if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < GRP; ++h) {
+            sm_m[warp][h] = st.m[h];
+            sm_l[warp][h] = st.l[h];
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < GRP; ++h)
+#pragma unroll
+        for (int i = 0; i < DL; ++i) sm_o[warp][h][lane * DL + i] = st.acc[h][i];
+}
+
+// Merges the published warp states of element e = (head h, dim dd): returns
+// the CTA's max M, sum Ls and unnormalised output O for it.
+template <int GRP, int D>
+__device__ __forceinline__ void decode_merge_warps(int h, int dd, const float (*sm_m)[GRP], const float (*sm_l)[GRP],
+                                                   const float (*sm_o)[GRP][D], float& M, float& Ls, float& O) {
+    M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_m[w][h]);
+    Ls = 0.f;
+    O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = exp2f(sm_m[w][h] - M);
+            Ls += sm_l[w][h] * f;
+            O += sm_o[w][h][dd] * f;
+        }
+    }
+}
+
+}  // namespace amcu

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "aethermind_b200.h"
+
 namespace amcu {
 
 constexpr int kNumSMs = 148;  // B200: 2 dies x 74 SMs
@@ -48,6 +50,15 @@ __device__ __forceinline__ uint4 ld_stream_u4(const void* p) {
 }
 __device__ __forceinline__ uint4 ld_u4(const void* p) {
     return *reinterpret_cast<const uint4*>(p);
+}
+
+// RoPE angle of pair i at position pos: inv_freq = 1 / theta^(2i/d) and the
+// angle in double, cos/sin rounded to float.
+__device__ __forceinline__ void rope_angle(double theta, int64_t d, int64_t pos, int64_t i, float& c, float& s) {
+    const double inv = 1.0 / pow(theta, 2.0 * (double)i / (double)d);
+    const double ang = (double)pos * inv;
+    c = (float)cos(ang);
+    s = (float)sin(ang);
 }
 
 // SiLU with the sign branch of the reference's const evaluator.
@@ -140,6 +151,27 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 // on). p 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// This CTA's share of an L2 prefetch hint: the ranges are split evenly over
+// the grid's CTAs (4 KB granules) and thread 0 requests its share in pieces
+// of at most 64 KB.
+__device__ __forceinline__ void l2_prefetch_share(const AmcuL2Prefetch& pf) {
+    if (threadIdx.x != 0) return;
+    const uint64_t nb = (uint64_t)gridDim.x * gridDim.y * gridDim.z;
+    const uint64_t b = blockIdx.x + (uint64_t)gridDim.x * (blockIdx.y + (uint64_t)gridDim.y * blockIdx.z);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const uint64_t bytes = pf.bytes[r] & ~(uint64_t)15;
+        if (pf.ptr[r] == nullptr || bytes == 0) continue;
+        const uint64_t per = ((bytes + nb - 1) / nb + 4095) & ~(uint64_t)4095;
+        const uint64_t begin = b * per;
+        const uint64_t end = begin + per < bytes ? begin + per : bytes;
+        for (uint64_t off = begin; off < end; off += 65536) {
+            const uint64_t n = end - off < 65536 ? end - off : 65536;
+            prefetch_l2_bulk(static_cast<const uint8_t*>(pf.ptr[r]) + off, (uint32_t)n);
+        }
+    }
 }
 
 // Orderable 32-bit key of a float (total order matching float <, NaN last).

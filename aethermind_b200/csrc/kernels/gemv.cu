@@ -1,26 +1,26 @@
 // Weight-only dequant GEMV for decode (m <= 8) and the weight prepacker.
 //
-// Device weight format ("tile16x64", K-chunked stream): the [N, K] weight is
-// cut into tiles of 16 output rows x 64 input columns. The tiles are stored in
-// the chunk-major stream order of stream_geom() (gemv.cuh): the K tiles of a
-// row block form kc chunks of tw tiles, and chunk w of every row block comes
-// before chunk w + 1, so tile (rb, c) sits at stream index
-// (c / tw * N/16 + rb) * tw + c % tw; tiles past K are zero. Inside a tile, lane L = 4g + t of a
-// warp owns rows {g, g+8} x columns [16t, 16t+16): exactly the A-operand
-// fragments of four m16n8k16 tensor-core MMAs in which MMA j contracts
-// columns 16t+4j .. 16t+4j+3 of this lane (the MMA's k-slot -> column map is a
-// free choice as long as the activation fragment uses the same one). One
-// 16-byte (INT4) or 32-byte (INT8) coalesced load per lane per tile feeds the
-// MMAs with no shuffles; the activations for the same columns are 32
-// contiguous bytes per lane.
-//   INT4 word j of lane L: nibble p at bits 4p, value +8 offset-binary is NOT
-//        used: nibbles hold two's-complement q. p0,p4,p2,p6 = row g columns
-//        +0,+1,+2,+3 and p1,p5,p3,p7 = row g+8 columns +0,+1,+2,+3, so
-//        (word >> 4i) & 0x000F000F yields MMA register i directly.
-//   INT8: 32 bytes per lane: row g columns [16t, 16t+16) then row g+8.
-//   INT4 scales: per tile pair of the stream (one 128-column group) 16 fp16,
-//        slot 2g = row g, 2g+1 = row g+8; zero for padding groups.
-//   INT8 scales: fp32 [N] (device row order).
+// Device weight format ("tile16x64"): the [N, K] weight is cut into tiles of
+// 16 output rows x 64 input columns, stored row block after row block with K
+// fastest. Inside a tile, lane L = 4g + t of a warp owns rows {g, g+8} x
+// columns [16t, 16t+16): exactly the A-operand fragments of four m16n8k16
+// tensor-core MMAs in which MMA j contracts columns 16t+4j .. 16t+4j+3 of this
+// lane (the MMA's k-slot -> column map is a free choice as long as the
+// activation fragment uses the same one). One 16-byte (INT4) or 32-byte
+// (INT8) conflict-free load per lane per tile feeds the MMAs with no
+// shuffles; the activations for the same columns are 32 contiguous bytes per
+// lane.
+//   INT4: the two tiles of a 128-column group and the group's 16 row scales
+//        form one 1056-byte pair record (tile 2p, tile 2p+1, 16 fp16 scales
+//        with slot 2g = row g, 2g+1 = row g+8), so one bulk copy brings
+//        weights and scales together; record (rb, p) at (rb * K/128 + p) *
+//        1056. Word j of lane L: nibble p at bits 4p holds two's-complement
+//        q; p0,p4,p2,p6 = row g columns +0,+1,+2,+3 and p1,p5,p3,p7 = row g+8
+//        columns +0,+1,+2,+3, so (word >> 4i) & 0x000F000F yields MMA
+//        register i directly.
+//   INT8: 1024-byte tiles, tile (rb, c) at (rb * K/64 + c) * 1024; 32 bytes
+//        per lane: row g columns [16t, 16t+16) then row g+8. Scales: fp32 [N]
+//        (device row order) in their own buffer.
 // Gate/up fusion: rows 0-7 of every tile are gate rows 8*rb..8*rb+7 and rows
 // 8-15 the matching up rows, so one lane holds gate and up of the same output
 // and the SiLU-Mul epilogue needs no data exchange.
@@ -38,22 +38,12 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// INT4 word -> 4 bf16x2 MMA registers holding the exact integers q.
-__device__ __forceinline__ void unpack_w4_word(uint32_t w, uint32_t (&a)[4]) {
-    // (w >> 4i) & 0x000F000F selects two nibbles; XOR with 0x43084308 maps the
-    // two's-complement nibble n to bf16 bits of 128 + (n ^ 8) = 136 + q
-    // (exact: integers up to 256 are representable); subtracting 136 gives q.
-    const uint32_t bias = 0x43084308u;  // bf16x2 (136, 136)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        uint32_t v;
-        const uint32_t s = w >> (4 * i);
-        asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(v) : "r"(s), "r"(0x000F000Fu), "r"(bias));  // (a & b) ^ c
-        __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
-        const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&bias);
-        h = __hsub2(h, b);
-        a[i] = *reinterpret_cast<uint32_t*>(&h);
-    }
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // Four int8 values -> two bf16x2 (bytes 0,1) and (bytes 2,3); exact.
@@ -74,9 +64,12 @@ __device__ __forceinline__ void unpack_w8_word(uint32_t w, uint32_t& lo, uint32_
 template <typename T>
 __device__ __forceinline__ T epi_store(float v) { return Act<T>::store(v); }
 
+// rm0 / rm1: exact power-of-two multipliers of activation rows 2t and 2t+1
+// (undo the staging's overflow guard).
 template <int FMT, int EPI>
-__device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int64_t rb, int g, int t, float4 s4) {
-    float acc[4] = {s4.x, s4.y, s4.z, s4.w};
+__device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int64_t rb, int g, int t, float4 s4, float rm0,
+                                              float rm1) {
+    float acc[4] = {s4.x * rm0, s4.y * rm1, s4.z * rm0, s4.w * rm1};
     __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
     const int m0 = 2 * t, m1 = 2 * t + 1;
     if constexpr (FMT == AMCU_WFMT_INT8) {
@@ -117,112 +110,147 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int64_t rb, i
     }
 }
 
-// Streaming GEMV. A CTA has one warp per K chunk of the stream layout and
-// owns `rb_per_cta` consecutive row blocks (16 output rows each). Warp w reads
-// one contiguous stream -- chunk w of the CTA's row blocks -- with a register
-// ring of kTwAlign tiles in flight: one coalesced 16-byte (INT4) or 32-byte
-// (INT8) load per lane per tile, issued kTwAlign tiles ahead with plain pointer
-// increments, no bounds checks (the stream's tail slack absorbs the last
-// read-ahead). The activations (m <= 8 rows, bf16) are staged once per CTA in
-// shared memory, zero-padded to the padded K.
+// Streaming GEMV. A CTA of 8 consumer warps and 1 producer warp owns
+// `rb_per_cta` consecutive row blocks (16 output rows each), one contiguous
+// run of the packed weight. The producer streams that run through a ring of
+// `stages` shared-memory stages with bulk copies (TMA engine) of 8-17 KB --
+// copies that small stop being able to keep HBM busy -- completing on one
+// mbarrier per stage; the consumers release a stage on a second mbarrier.
+// The first stages are requested before the kernel waits for its
+// predecessor. In a stage the consumer warps split the 128-column groups
+// (INT4 pair records, INT8 tile pairs) and read their tiles with one
+// conflict-free shared load per lane per tile. The activations (m <= 8 rows,
+// bf16) are staged once per CTA in shared memory.
 //
-// INT4 tiles are fed to the MMA as the exact bf16 integers 136 + q (one LOP3
-// per register from the packed nibbles); the offset is removed after the MMA
-// by subtracting 136 * sum(x) over each 128-column group, sums computed once
-// per CTA into shared memory. Products (136 + q) * x are exact in fp32, so the
-// correction costs only fp32 rounding.
+// INT4 tiles go to fp16 MMAs as exact integers with an offset: one LOP3
+// selects two nibbles and ORs in the fp16 exponent of 1024, giving 1032 + q
+// for nibbles in bits 0-3 of each half (rows g) and 1152 + 16q for nibbles in
+// bits 4-7 (rows g+8), so a 32-bit word costs four LOP3 and one shift. The
+// offsets are removed after the MMA with the per-group sums of x (computed
+// once per CTA) and the 16 is folded into the row's scale. The activations
+// are staged as fp16 for this: converting bf16 to fp16 is exact in fp16's
+// normal range, and a row whose magnitude would overflow fp16 is staged
+// multiplied by an exact power of two that the epilogue takes back out.
+// Products (offset + q) * x are exact in fp32, so the offsets cost only fp32
+// rounding.
 //
 // At the end of a row block the warps' 16 x 8 partial tiles meet in shared
 // memory (double-buffered, one barrier) and one warp applies the epilogue.
 constexpr int kXPad = 16;  // bytes of padding per staged activation row
 #ifndef GEMV_MINB
-#define GEMV_MINB 4
+#define GEMV_MINB 2
 #endif
-// Row blocks of its stream that a warp keeps requested into L2 ahead of the
-// one it is reading (bulk L2 prefetch; 0 turns the prefetch off).
-#ifndef GEMV_PW
-#define GEMV_PW 2
+// CTAs per SM the launcher sizes the rings for.
+#ifndef GEMV_CPS
+#define GEMV_CPS 2
 #endif
 
-// (q + 136) in bf16: (w >> 4i) & 0x000F000F selects two nibbles, XOR with
-// 0x43084308 gives bf16 bits of 128 + (n ^ 8) = 136 + q (exact).
-__device__ __forceinline__ void unpack_w4_word_biased(uint32_t w, uint32_t (&a)[4]) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(a[i]) : "r"(w >> (4 * i)), "r"(0x000F000Fu), "r"(0x43084308u));
+// INT4 word -> fp16 MMA registers: a0/a2 = 1032 + q (bits 0-3, 8-11 of each
+// half: rows g), a1/a3 = 1152 + 16q (bits 4-7, 12-15: rows g+8). (w & mask)
+// ^ c flips the nibble's sign bit (n ^ 8 = q + 8) and sets exponent 1024.
+__device__ __forceinline__ void unpack_w4_word_f16(uint32_t w, uint32_t (&a)[4]) {
+    const uint32_t w8 = w >> 8;
+    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(a[0]) : "r"(w), "r"(0x000F000Fu), "r"(0x64086408u));
+    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(a[1]) : "r"(w), "r"(0x00F000F0u), "r"(0x64806480u));
+    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(a[2]) : "r"(w8), "r"(0x000F000Fu), "r"(0x64086408u));
+    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(a[3]) : "r"(w8), "r"(0x00F000F0u), "r"(0x64806480u));
 }
 
+// Shared memory carve-up (bytes; every part 128-byte aligned).
+struct GemvSmem {
+    int red, sx, xs, ring, bars, total;
+};
 template <int FMT>
-__host__ __device__ constexpr int tile_bytes() { return FMT == AMCU_WFMT_INT4 ? 512 : 1024; }
+__host__ __device__ inline GemvSmem gemv_smem(int m, int64_t k, int stage_bytes, int stages) {
+    auto up = [](int64_t v) { return (int)((v + 127) / 128 * 128); };
+    GemvSmem s;
+    s.red = 0;
+    s.sx = up(2 * kGemvConsumers * 32 * 16);
+    s.xs = s.sx + up(FMT == AMCU_WFMT_INT4 ? (k / 128) * 8 * 4 : 0);
+    s.ring = s.xs + up(m * (k * 2 + kXPad));
+    s.bars = s.ring + stages * stage_bytes;
+    s.total = s.bars + up(2 * stages * 8);
+    return s;
+}
 
 template <int FMT, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvParams p) {
-    constexpr int TB = tile_bytes<FMT>();
-    constexpr int NV = TB / 512;  // uint4 per lane per tile
-    constexpr int D = kTwAlign;   // ring depth; tw is a multiple of it
     constexpr bool W4 = FMT == AMCU_WFMT_INT4;
-    extern __shared__ __align__(16) uint8_t smem[];
+    constexpr int UB = W4 ? kW4PairBytes : 2048;  // bytes per 128-column group unit
+    extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int nw = p.kc, tw = p.tw;
-    const int kp = nw * tw * 64;  // padded K
-    const int gp = kp / 128;      // padded groups (INT4)
+    const int S = p.stages, SU = p.stage_units;  // stages; group units per stage
+    const int SBY = SU * UB;                     // bytes per stage
+    const int G = (int)(p.k / 128);              // group units per row block
     const int M = (int)p.m;
-    const int xrow = kp * 2 + kXPad;
-    float4* red = reinterpret_cast<float4*>(smem);                      // [2][nw][32]
-    float* sx = reinterpret_cast<float*>(smem + 2 * nw * 32 * 16);      // [gp][8] (INT4)
-    uint8_t* xs = smem + 2 * nw * 32 * 16 + (W4 ? gp * 8 * 4 : 0);      // [M][kp] bf16 (+pad)
+    const int xrow = (int)(p.k * 2 + kXPad);
+    const GemvSmem L = gemv_smem<FMT>(M, p.k, SBY, S);
+    float4* red = reinterpret_cast<float4*>(smem + L.red);  // [2][consumers][32]
+    float* sx = reinterpret_cast<float*>(smem + L.sx);      // [G][8] (INT4)
+    uint8_t* xs = smem + L.xs;                              // [M][k] bf16 (+pad)
+    uint8_t* ring = smem + L.ring;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+    uint64_t* empty = full + S;
 
     const int nrb = (int)(p.n / 16);
     const int rb0 = blockIdx.x * p.rb_per_cta;
     const int nr = (rb0 + p.rb_per_cta < nrb ? rb0 + p.rb_per_cta : nrb) - rb0;
+    const int per_row = G / SU;  // stages per row block
+    const int total = nr * per_row;
+    const uint8_t* run = static_cast<const uint8_t*>(p.w) + (size_t)rb0 * G * UB;
 
-    // this warp's stream: chunk `warp` of row blocks rb0 .. rb0 + nr
-    const size_t s0 = ((size_t)warp * nrb + rb0) * tw;  // first tile
-    const uint8_t* wbase = static_cast<const uint8_t*>(p.w) + s0 * TB;
-    const uint8_t* sbase = static_cast<const uint8_t*>(p.scales) + s0 / 2 * 32;  // INT4: 32 B per tile pair
-    auto prefetch_row = [&](int r) {
-        if (GEMV_PW > 0 && lane == 0 && r < nr) {
-            prefetch_l2_bulk(wbase + (size_t)r * tw * TB, (uint32_t)(tw * TB));
-            if constexpr (W4) prefetch_l2_bulk(sbase + (size_t)r * tw / 2 * 32, (uint32_t)(tw / 2 * 32));
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kGemvConsumers);
         }
-    };
-#pragma unroll
-    for (int r = 0; r < GEMV_PW; ++r) prefetch_row(r);
-
-    const uint8_t* wp = wbase + lane * 16 * NV;
-    const uint8_t* sp = sbase + 4 * g;
-    uint4 wbuf[D][NV];
-    uint32_t sbuf[D / 2];
-#pragma unroll
-    for (int u = 0; u < D; ++u) {
-#pragma unroll
-        for (int v = 0; v < NV; ++v) wbuf[u][v] = ld_stream_u4(wp + u * TB + 16 * v);
-        if (W4 && (u & 1) == 0) sbuf[u / 2] = __ldg(reinterpret_cast<const unsigned int*>(sp + (u / 2) * 32));
+        fence_mbar_init();
+        l2_prefetch_share(p.l2_next);
     }
-    wp += D * TB;
-    sp += (D / 2) * 32;
+    __syncthreads();
 
-    // Weights do not depend on earlier kernels; the activations do.
+    if (warp == kGemvConsumers) {
+        // ---- producer: weights do not depend on earlier kernels, so the ring
+        // fills while the previous kernel finishes.
+        if (lane == 0) {
+            int slot = 0;
+            uint32_t phase = 0;
+            for (int i = 0; i < total; ++i) {
+                if (i >= S && !mbar_wait(&empty[slot], phase ^ 1u)) {
+                    record_device_error(p.err, kErrGemvEmptyWait);
+                    break;
+                }
+                mbar_expect_tx(&full[slot], SBY);
+                bulk_g2s(ring + slot * SBY, run + (size_t)i * SBY, SBY, &full[slot]);
+                if (++slot == S) {
+                    slot = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+        return;
+    }
+
     pdl_wait();
     pdl_trigger();
 
-    // ---- stage activations [m][kp] (+16 B per row, zero beyond k) and, for INT4, per-group sums of x
+    // ---- stage activations [m][k] (+16 B per row) and, for INT4, per-group sums of x
+    constexpr int NT = kGemvConsumers * 32;
     {
-        const int chunks = kp / 8, real = (int)(p.k / 8);
+        const int chunks = (int)(p.k / 8);
         const __nv_bfloat16* xg = static_cast<const __nv_bfloat16*>(p.x);
-        for (int i = threadIdx.x; i < M * chunks; i += blockDim.x) {
+        for (int i = threadIdx.x; i < M * chunks; i += NT) {
             const int m = i / chunks, c = i - m * chunks;
-            *reinterpret_cast<uint4*>(xs + m * xrow + c * 16) =
-                    c < real ? ld_u4(xg + m * p.x_stride + c * 8) : make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(xs + m * xrow + c * 16) = ld_u4(xg + m * p.x_stride + c * 8);
         }
     }
-    __syncthreads();
+    named_bar_sync(2, NT);
     if (p.norm_w) {
-        // fused RMSNorm of the staged rows: warp w owns rows w, w + nw, ... as
+        // fused RMSNorm of the staged rows: warp w owns rows w, w + 8, ... as
         // y = round(x * (mean(x^2) + eps)^-1/2 * w) (the RMSNorm kernel's formula)
         float* inv_s = reinterpret_cast<float*>(red);  // red is free until the first row-block end
-        for (int m = warp; m < M; m += nw) {
+        for (int m = warp; m < M; m += kGemvConsumers) {
             const uint8_t* xr = xs + m * xrow;
             float ss = 0.f;
             for (int c = lane; c < (int)(p.k / 8); c += 32) {
@@ -237,10 +265,10 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
             ss = warp_sum(ss);
             if (lane == 0) inv_s[m] = 1.0f / sqrtf(ss / (float)p.k + p.eps);
         }
-        __syncthreads();
+        named_bar_sync(2, NT);
         const int chunks = (int)(p.k / 8);
         const __nv_bfloat16* nwt = static_cast<const __nv_bfloat16*>(p.norm_w);
-        for (int i = threadIdx.x; i < M * chunks; i += blockDim.x) {
+        for (int i = threadIdx.x; i < M * chunks; i += NT) {
             const int m = i / chunks, c = i - m * chunks;
             uint4* xp = reinterpret_cast<uint4*>(xs + m * xrow + c * 16);
             const uint4 v = *xp, wv = ld_u4(nwt + c * 8);
@@ -256,111 +284,188 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
             }
             *xp = make_uint4(o[0], o[1], o[2], o[3]);
         }
-        __syncthreads();
+        named_bar_sync(2, NT);
     }
+    __shared__ float row_mul[kGemvMaxM];  // epilogue multiplier per activation row
     if constexpr (W4) {
-        const int segs = gp * 8 * M;  // 16-column segments, 8 per group
-        for (int s0i = 0; s0i < segs; s0i += blockDim.x) {
-            const int s = s0i + threadIdx.x;
+        // Overflow guard for the fp16 staging: rows with max |x| > 2^15 are
+        // scaled by 2^-e (exact) and the epilogue multiplies by 2^e.
+        __shared__ unsigned int row_amax[kGemvMaxM];
+        if (threadIdx.x < kGemvMaxM) row_amax[threadIdx.x] = 0u;
+        named_bar_sync(2, NT);
+        {
+            const int chunks = (int)(p.k / 8);
+            for (int i = threadIdx.x; i < M * chunks; i += NT) {
+                const int m = i / chunks, c = i - m * chunks;
+                const uint4 v = *reinterpret_cast<const uint4*>(xs + m * xrow + c * 16);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                uint32_t mx = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) mx = max(mx, max((w[j] << 16) & 0x7fffffffu, w[j] & 0x7fff0000u));
+                if (mx > 0x47000000u) atomicMax(&row_amax[m], mx);  // only rows above 2^15 matter
+            }
+        }
+        named_bar_sync(2, NT);
+        if (threadIdx.x < kGemvMaxM) {
+            const unsigned int mx = row_amax[threadIdx.x];
+            // e = exponent(max) - 15 for max >= 2^15 (one more keeps the rounded max below 2^16)
+            const int e = mx > 0x47000000u ? (int)((mx >> 23) & 0xff) - 127 - 15 + 1 : 0;
+            row_mul[threadIdx.x] = __int_as_float((127 + e) << 23);
+        }
+        named_bar_sync(2, NT);
+        // convert to fp16 in place (times 2^-e) and sum each 128-column group
+        const int segs = G * 8 * M;  // 16-column segments, 8 per group
+        for (int s0 = 0; s0 < segs; s0 += NT) {
+            const int s = s0 + threadIdx.x;
             float sum = 0.f;
             int m = 0, grp = 0;
             if (s < segs) {
-                m = s / (gp * 8);
-                const int r = s - m * gp * 8;
+                m = s / (G * 8);
+                const int r = s - m * G * 8;
                 grp = r >> 3;
-                const uint8_t* xp = xs + m * xrow + (grp * 128 + (r & 7) * 16) * 2;
-                const uint4 a = *reinterpret_cast<const uint4*>(xp), b = *reinterpret_cast<const uint4*>(xp + 16);
+                uint4* xp = reinterpret_cast<uint4*>(xs + m * xrow + (grp * 128 + (r & 7) * 16) * 2);
+                const float inv = 1.0f / row_mul[m];  // exact: a power of two
+                const uint4 a = xp[0], b = xp[1];
                 const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                uint32_t h[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) sum += __uint_as_float(w[j] << 16) + __uint_as_float(w[j] & 0xffff0000u);
+                for (int j = 0; j < 8; ++j) {
+                    const __half2 v = __floats2half2_rn(__uint_as_float(w[j] << 16) * inv,
+                                                        __uint_as_float(w[j] & 0xffff0000u) * inv);
+                    sum += __low2float(v) + __high2float(v);
+                    h[j] = *reinterpret_cast<const uint32_t*>(&v);
+                }
+                xp[0] = make_uint4(h[0], h[1], h[2], h[3]);
+                xp[1] = make_uint4(h[4], h[5], h[6], h[7]);
             }
             sum += __shfl_xor_sync(0xffffffffu, sum, 1);
             sum += __shfl_xor_sync(0xffffffffu, sum, 2);
             sum += __shfl_xor_sync(0xffffffffu, sum, 4);
             if (s < segs && (s & 7) == 0) sx[grp * 8 + m] = sum;
         }
-        for (int i = threadIdx.x; i < gp * 8; i += blockDim.x)
+        for (int i = threadIdx.x; i < G * 8; i += NT)
             if ((i & 7) >= M) sx[i] = 0.f;  // rows without activations add nothing
-        __syncthreads();
+        named_bar_sync(2, NT);
+    } else {
+        if (threadIdx.x < kGemvMaxM) row_mul[threadIdx.x] = 1.f;
+        named_bar_sync(2, NT);
     }
+    const float rm0 = 2 * t < M ? row_mul[2 * t] : 1.f, rm1 = 2 * t + 1 < M ? row_mul[2 * t + 1] : 1.f;
 
     // Lanes whose activation row does not exist (g >= M) read row 0: they only
     // feed MMA output columns g >= M, which the epilogue never stores.
-    const uint8_t* xw = xs + (g < M ? g : 0) * xrow + (warp * tw * 64 + 16 * t) * 2;  // + 128 B per tile
-    const float* sxw = sx + (warp * tw / 2) * 8 + 2 * t;                               // + 8 floats per group
+    const uint8_t* xrow_g = xs + (g < M ? g : 0) * xrow + 32 * t;  // + 256 B per group unit
+    int slot = 0;
+    uint32_t phase = 0;
+    bool ok = true;  // false once a wait ran out: keep the control flow, skip further waits
+    int fail_i = -1;
     int par = 0;
     for (int r = 0; r < nr; ++r, par ^= 1) {
-        prefetch_row(r + GEMV_PW);
-        const uint8_t* xp = xw;
-        const float* sxp = sxw;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int j = 0; j < tw; j += D, xp += D * 128, sxp += (D / 2) * 8, wp += D * TB, sp += (D / 2) * 32) {
-#pragma unroll
-            for (int u = 0; u < D; u += 2) {
-                float part[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int j = 0; j < per_row; ++j) {
+            const int i = r * per_row + j;
+            if (ok && !mbar_wait(&full[slot], phase)) {
+                ok = false;
+                fail_i = i;
+                if (lane == 0) record_device_error(p.err, kErrGemvFullWait);
+            }
+            const uint8_t* st = ring + slot * SBY;
+            for (int u = warp; u < SU; u += kGemvConsumers) {  // this warp's group units of the stage
+                const int grp = j * SU + u;                       // group within the row block
+                const uint8_t* rec = st + u * UB;
+                const uint8_t* xp = xrow_g + grp * 256;
+                float part[2][4];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const uint4 x0 = *reinterpret_cast<const uint4*>(xp + (u + h) * 128);
-                    const uint4 x1 = *reinterpret_cast<const uint4*>(xp + (u + h) * 128 + 16);
-                    const uint32_t X[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                    if constexpr (W4) {
-                        const uint32_t words[4] = {wbuf[u + h][0].x, wbuf[u + h][0].y, wbuf[u + h][0].z,
-                                                   wbuf[u + h][0].w};
 #pragma unroll
-                        for (int jj = 0; jj < 4; ++jj) {
-                            uint32_t a[4];
-                            unpack_w4_word_biased(words[jj], a);
-                            mma_bf16_16816(part, a, X[2 * jj], X[2 * jj + 1]);
-                        }
+                    for (int e = 0; e < 4; ++e) part[h][e] = 0.f;
+                    const uint4 x0 = *reinterpret_cast<const uint4*>(xp + h * 128);
+                    const uint4 x1 = *reinterpret_cast<const uint4*>(xp + h * 128 + 16);
+                    if constexpr (W4) {
+                        const uint4 wv = *reinterpret_cast<const uint4*>(rec + h * 512 + lane * 16);
+                        uint32_t a[4];
+                        unpack_w4_word_f16(wv.x, a);
+                        mma_f16_16816(part[h], a, x0.x, x0.y);
+                        unpack_w4_word_f16(wv.y, a);
+                        mma_f16_16816(part[h], a, x0.z, x0.w);
+                        unpack_w4_word_f16(wv.z, a);
+                        mma_f16_16816(part[h], a, x1.x, x1.y);
+                        unpack_w4_word_f16(wv.w, a);
+                        mma_f16_16816(part[h], a, x1.z, x1.w);
                     } else {
-                        const uint32_t rg[4] = {wbuf[u + h][0].x, wbuf[u + h][0].y, wbuf[u + h][0].z,
-                                                wbuf[u + h][0].w};
-                        const uint32_t rh[4] = {wbuf[u + h][1].x, wbuf[u + h][1].y, wbuf[u + h][1].z,
-                                                wbuf[u + h][1].w};
+                        const uint4 va = *reinterpret_cast<const uint4*>(rec + h * 1024 + lane * 32);
+                        const uint4 vb = *reinterpret_cast<const uint4*>(rec + h * 1024 + lane * 32 + 16);
+                        const uint32_t rg[4] = {va.x, va.y, va.z, va.w};
+                        const uint32_t rh[4] = {vb.x, vb.y, vb.z, vb.w};
+                        const uint32_t X[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
                         for (int jj = 0; jj < 4; ++jj) {
                             uint32_t a[4];
                             unpack_w8_word(rg[jj], a[0], a[2]);
                             unpack_w8_word(rh[jj], a[1], a[3]);
-                            mma_bf16_16816(acc, a, X[2 * jj], X[2 * jj + 1]);
+                            mma_bf16_16816(part[h], a, X[2 * jj], X[2 * jj + 1]);
                         }
                     }
-#pragma unroll
-                    for (int v = 0; v < NV; ++v) wbuf[u + h][v] = ld_stream_u4(wp + (u + h) * TB + 16 * v);
                 }
                 if constexpr (W4) {
-                    // part holds sum (136 + q) x over the group's 128 columns
-                    const float2 s2x = *reinterpret_cast<const float2*>(sxp + (u / 2) * 8);
-                    const __half2 s2 = *reinterpret_cast<const __half2*>(&sbuf[u / 2]);
-                    const float s_lo = __low2float(s2), s_hi = __high2float(s2);
-                    acc[0] = fmaf(fmaf(-136.f, s2x.x, part[0]), s_lo, acc[0]);
-                    acc[1] = fmaf(fmaf(-136.f, s2x.y, part[1]), s_lo, acc[1]);
-                    acc[2] = fmaf(fmaf(-136.f, s2x.x, part[2]), s_hi, acc[2]);
-                    acc[3] = fmaf(fmaf(-136.f, s2x.y, part[3]), s_hi, acc[3]);
-                    sbuf[u / 2] = __ldg(reinterpret_cast<const unsigned int*>(sp + (u / 2) * 32));
+                    // part[0] + part[1] hold sum (1032 + q) x (rows g) and
+                    // sum (1152 + 16q) x (rows g+8) over the group's 128 columns
+                    const float2 s2x = *reinterpret_cast<const float2*>(sx + grp * 8 + 2 * t);
+                    const uint32_t sv = *reinterpret_cast<const uint32_t*>(rec + 1024 + 4 * g);
+                    const __half2 s2 = *reinterpret_cast<const __half2*>(&sv);
+                    const float s_lo = __low2float(s2), s_hi = __high2float(s2) * 0.0625f;
+                    acc[0] = fmaf(fmaf(-1032.f, s2x.x, part[0][0] + part[1][0]), s_lo, acc[0]);
+                    acc[1] = fmaf(fmaf(-1032.f, s2x.y, part[0][1] + part[1][1]), s_lo, acc[1]);
+                    acc[2] = fmaf(fmaf(-1152.f, s2x.x, part[0][2] + part[1][2]), s_hi, acc[2]);
+                    acc[3] = fmaf(fmaf(-1152.f, s2x.y, part[0][3] + part[1][3]), s_hi, acc[3]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) acc[e] += part[0][e] + part[1][e];
                 }
+            }
+            __syncwarp();  // every lane has read the stage
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == S) {
+                slot = 0;
+                phase ^= 1;
             }
         }
         // row-block end: publish this warp's partial tile, meet the other
         // warps, and let one warp reduce and apply the epilogue
-        red[(par * nw + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        named_bar_sync(1, nw * 32);
+        red[(par * kGemvConsumers + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        named_bar_sync(1, NT);
         const int rb = rb0 + r;
-        if (warp == rb % nw) {
+        if (warp == rb % kGemvConsumers) {
             float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int w = 0; w < nw; ++w) {
-                const float4 v = red[(par * nw + w) * 32 + lane];
+#pragma unroll
+            for (int w = 0; w < kGemvConsumers; ++w) {
+                const float4 v = red[(par * kGemvConsumers + w) * 32 + lane];
                 s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
             }
-            gemv_epilogue<FMT, EPI>(p, rb, g, t, s4);
+            gemv_epilogue<FMT, EPI>(p, rb, g, t, s4, rm0, rm1);
         }
+    }
+    if (fail_i >= 0 && warp == 0 && lane == 0) {
+        // A wait ran out: stages fail_i .. total - 1 may still be landing.
+        // Give them a bounded chance before the CTA's shared memory goes away.
+        for (int k = fail_i; k < total; ++k)
+            if (!mbar_wait(&full[k % S], (uint32_t)(k / S) & 1u)) {
+                record_device_error(p.err, kErrGemvDrain);
+                break;
+            }
     }
 }
 
 template <int FMT>
-static size_t gemv_smem_bytes(int64_t m, const StreamGeom& sg) {
-    const int64_t kp = (int64_t)sg.kc * sg.tw * 64;
-    return 2 * sg.kc * 32 * 16 + (FMT == AMCU_WFMT_INT4 ? (kp / 128) * 8 * 4 : 0) + m * (kp * 2 + kXPad);
+static int stage_units(int64_t k) {
+    // group units per stage: the largest divisor of k/128 that keeps a stage
+    // at most kMaxStageBytes (INT4: 16 pair records = 16.5 KB; INT8: 8 tile
+    // pairs = 16 KB)
+    const int G = (int)(k / 128), cap = FMT == AMCU_WFMT_INT4 ? 16 : 8;
+    int best = 1;
+    for (int d = 1; d <= cap; ++d)
+        if (G % d == 0) best = d;
+    return best;
 }
 
 // Plain fp32 weights (the fp32 tiny model): one thread per output, fp32 FMA.
@@ -396,33 +501,41 @@ __global__ void gemm_plain_kernel(GemvParams p) {
 template <int FMT, int EPI>
 static void launch_gemv_one(GemvParams p, cudaStream_t s) {
     constexpr int kMaxSmem = 200 * 1024;
-    static int per_sm[9] = {};  // resident CTAs per SM by warps per CTA (one device per process on this path)
-    const StreamGeom sg = stream_geom(p.k);
-    if (per_sm[sg.kc] == 0) {
+    static int smem_per_sm = 0;
+    if (smem_per_sm == 0) {
+        int dev = 0, v = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        smem_per_sm = v > 0 ? v : 228 * 1024;
         cudaFuncSetAttribute(gemv_tc_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-        int n = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_tc_kernel<FMT, EPI>, 32 * sg.kc,
-                                                      gemv_smem_bytes<FMT>(1, sg));
-        per_sm[sg.kc] = n > 0 ? n : 1;
     }
-    const int64_t max_ctas = (int64_t)per_sm[sg.kc] * num_sms();
+    constexpr int UB = FMT == AMCU_WFMT_INT4 ? kW4PairBytes : 2048;
+    const int su = stage_units<FMT>(p.k);
+    const int sby = su * UB;
+    // Ring stages: as many (2..8) as keep GEMV_CPS CTAs resident per SM with
+    // one activation row.
+    const int per_cta = smem_per_sm / GEMV_CPS - 2048;  // room for the per-CTA reserve
+    int stages = 8;
+    while (stages > 2 && gemv_smem<FMT>(1, p.k, sby, stages).total > per_cta) --stages;
+    p.stages = stages;
+    p.stage_units = su;
+    const int per_sm = smem_per_sm / (gemv_smem<FMT>(1, p.k, sby, stages).total + 1024);
+    const int64_t max_ctas = (int64_t)(per_sm > 0 ? per_sm : 1) * num_sms();
     const int64_t nrb = p.n / 16;
-    p.kc = sg.kc;
-    p.tw = sg.tw;
     p.rb_per_cta = (int)((nrb + max_ctas - 1) / max_ctas);
     const int64_t grid = (nrb + p.rb_per_cta - 1) / p.rb_per_cta;
     // The activation rows are staged in shared memory; when m rows of this K do
-    // not fit, the rows go in slices (each slice streams W again).
+    // not fit next to the ring, the rows go in slices (each slice streams W again).
     int64_t fit = p.m;
-    while (fit > 1 && gemv_smem_bytes<FMT>(fit, sg) > (size_t)kMaxSmem) --fit;
+    while (fit > 1 && gemv_smem<FMT>((int)fit, p.k, sby, stages).total > kMaxSmem) --fit;
     for (int64_t m0 = 0; m0 < p.m; m0 += fit) {
         GemvParams q = p;
         q.m = p.m - m0 < fit ? p.m - m0 : fit;
         q.x = static_cast<const __nv_bfloat16*>(p.x) + m0 * p.x_stride;
         q.y = static_cast<__nv_bfloat16*>(p.y) + m0 * p.y_stride;
         if (p.residual) q.residual = static_cast<const __nv_bfloat16*>(p.residual) + m0 * p.y_stride;
-        launch_pdl(gemv_tc_kernel<FMT, EPI>, dim3((unsigned)grid), dim3(32 * sg.kc), gemv_smem_bytes<FMT>(q.m, sg),
-                   s, q);
+        launch_pdl(gemv_tc_kernel<FMT, EPI>, dim3((unsigned)grid), dim3(kGemvThreads),
+                   (size_t)gemv_smem<FMT>((int)q.m, p.k, sby, stages).total, s, q);
     }
 }
 
@@ -468,57 +581,58 @@ __device__ __forceinline__ int64_t src_row(int64_t r, bool il, int& which) {
     return rb * 8 + (rr & 7);
 }
 
-// Where the packers write: the source rows are row blocks [0, nrb) of a
-// canonical matrix; they go to row blocks [rb0, rb0 + nrb) of a stream with
-// nrb_total row blocks (a fused weight packs its parts one after another).
-struct PackGeom {
-    int64_t nrb, nrb_total, rb0;
-    int kc, tw;
-};
-struct TilePos {
-    int64_t rb, c;  // source row block and K tile (c >= K/64: padding)
-    int64_t dst;    // stream tile index
-};
-// Tile `ti` of the part, counted chunk-major like the stream itself.
-__device__ __forceinline__ TilePos part_tile(int64_t ti, const PackGeom& pg) {
-    const int64_t cc = ti % pg.tw, rest = ti / pg.tw;
-    const int64_t rb = rest % pg.nrb, w = rest / pg.nrb;
-    return TilePos{rb, w * pg.tw + cc, (w * pg.nrb_total + pg.rb0 + rb) * pg.tw + cc};
-}
-
-// INT4: one thread per 32-bit device word of the part.
-__global__ void pack_w4_kernel(const uint8_t* __restrict__ a, const uint8_t* __restrict__ b, bool il,
-                               int64_t K, PackGeom pg, uint32_t* __restrict__ out, bool unpack,
-                               uint8_t* __restrict__ canon_out) {
-    const int64_t C = K / 64;
-    const int64_t words = (int64_t)pg.kc * pg.nrb * pg.tw * 128;
-    for (int64_t wi = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; wi < words; wi += (int64_t)gridDim.x * blockDim.x) {
-        const TilePos tp = part_tile(wi / 128, pg);  // 512 B per tile = 128 words
-        const int in_tile = (int)(wi % 128);
+// INT4: one thread per 32-bit word of a tile or of a pair record's scales.
+// Rows of the source part go to row blocks [rb0, rb0 + N/16) of the packed
+// weight (a fused weight packs its parts one after another).
+__global__ void pack_w4_kernel(const uint8_t* __restrict__ a, const uint8_t* __restrict__ b, const __half* sa,
+                               const __half* sb, bool il, int64_t N, int64_t K, int64_t rb0,
+                               uint32_t* __restrict__ out, bool unpack, uint8_t* __restrict__ canon_out,
+                               __half* __restrict__ canon_s) {
+    const int64_t G = K / 128;
+    constexpr int kWords = kW4PairBytes / 4;  // 264: 2 x 128 tile words + 8 scale words
+    const int64_t total = N / 16 * G * kWords;
+    for (int64_t wi = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; wi < total;
+         wi += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t rec = wi / kWords;  // (row block, group) of the part
+        const int in_rec = (int)(wi % kWords);
+        const int64_t rb = rec / G, grp = rec % G;
+        uint32_t* dst = out + ((rb0 + rb) * G + grp) * kWords + in_rec;
+        if (in_rec >= 256) {  // scales: word s holds slots 2s, 2s+1 = rows s, s+8
+            const int gg = in_rec - 256;
+            const int64_t rlo = rb * 16 + gg, rhi = rlo + 8;
+            if (!unpack) {
+                int wl, wh;
+                const int64_t slo = src_row(rlo, il, wl), shi = src_row(rhi, il, wh);
+                const __half hl = (wl ? sb : sa)[slo * G + grp], hh = (wh ? sb : sa)[shi * G + grp];
+                *dst = (uint32_t)__half_as_ushort(hl) | ((uint32_t)__half_as_ushort(hh) << 16);
+            } else if (canon_s) {
+                const uint32_t v = *dst;
+                canon_s[rlo * G + grp] = __ushort_as_half((unsigned short)(v & 0xffffu));
+                canon_s[rhi * G + grp] = __ushort_as_half((unsigned short)(v >> 16));
+            }
+            continue;
+        }
+        const int h = in_rec >> 7, in_tile = in_rec & 127;
         const int lane = in_tile >> 2, j = in_tile & 3;
         const int g = lane >> 2, t = lane & 3;
-        const int64_t rb = tp.rb, c = tp.c;
-        const int64_t col0 = c * 64 + 16 * t + 4 * j;
-        uint32_t* dst = out + tp.dst * 128 + in_tile;
+        const int64_t col0 = grp * 128 + h * 64 + 16 * t + 4 * j;
         // nibble p -> (row offset, column offset)
         const int prow[8] = {0, 8, 0, 8, 0, 8, 0, 8};
         const int pcol[8] = {0, 0, 2, 2, 1, 1, 3, 3};
         if (!unpack) {
             uint32_t word = 0;
-            if (c < C) {
 #pragma unroll
-                for (int pp = 0; pp < 8; ++pp) {
-                    int which;
-                    const int64_t r = src_row(rb * 16 + g + prow[pp], il, which);
-                    const uint8_t* src = which ? b : a;
-                    const int64_t col = col0 + pcol[pp];
-                    const uint8_t byte = src[r * (K / 2) + col / 2];
-                    const uint32_t nib = (col & 1) ? (byte >> 4) : (byte & 15u);
-                    word |= nib << (4 * pp);
-                }
+            for (int pp = 0; pp < 8; ++pp) {
+                int which;
+                const int64_t r = src_row(rb * 16 + g + prow[pp], il, which);
+                const uint8_t* src = which ? b : a;
+                const int64_t col = col0 + pcol[pp];
+                const uint8_t byte = src[r * (K / 2) + col / 2];
+                const uint32_t nib = (col & 1) ? (byte >> 4) : (byte & 15u);
+                word |= nib << (4 * pp);
             }
             *dst = word;
-        } else if (c < C) {
+        } else {
             const uint32_t word = *dst;
 #pragma unroll
             for (int pp = 0; pp < 4; ++pp) {
@@ -532,54 +646,25 @@ __global__ void pack_w4_kernel(const uint8_t* __restrict__ a, const uint8_t* __r
     }
 }
 
-// INT4 scales: canonical fp16 [N][G] -> per stream tile pair 16 halves, slot
-// 2g = row g, 2g+1 = row g+8 (zero for padding groups).
-__global__ void pack_s4_kernel(const __half* __restrict__ a, const __half* __restrict__ b, bool il, int64_t G,
-                               PackGeom pg, __half* __restrict__ out, bool unpack) {
-    const int64_t pairs = (int64_t)pg.kc * pg.nrb * (pg.tw / 2);
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < pairs * 16;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int slot = (int)(i % 16);
-        const TilePos tp = part_tile(i / 16 * 2, pg);  // first tile of the pair
-        const int64_t grp = tp.c / 2;
-        const int64_t r_dev = tp.rb * 16 + (slot >> 1) + ((slot & 1) ? 8 : 0);
-        __half* dst = out + tp.dst / 2 * 16 + slot;
-        if (!unpack) {
-            if (grp < G) {
-                int which;
-                const int64_t r = src_row(r_dev, il, which);
-                *dst = (which ? b : a)[r * G + grp];
-            } else {
-                *dst = __float2half(0.f);
-            }
-        } else if (grp < G) {
-            const_cast<__half*>(a)[r_dev * G + grp] = *dst;
-        }
-    }
-}
-
-// INT8: one thread per 16-byte half-lane chunk of the part.
-__global__ void pack_w8_kernel(const int8_t* __restrict__ a, const int8_t* __restrict__ b, bool il, int64_t K,
-                               PackGeom pg, uint4* __restrict__ out, bool unpack) {
+// INT8: one thread per 16-byte half-lane chunk.
+__global__ void pack_w8_kernel(const int8_t* __restrict__ a, const int8_t* __restrict__ b, bool il, int64_t N,
+                               int64_t K, int64_t rb0, uint4* __restrict__ out, bool unpack) {
+    const int64_t chunks = N * K / 16;
     const int64_t C = K / 64;
-    const int64_t chunks = (int64_t)pg.kc * pg.nrb * pg.tw * 64;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < chunks; i += (int64_t)gridDim.x * blockDim.x) {
-        const TilePos tp = part_tile(i / 64, pg);  // 1024 B per tile
+        const int64_t tile = i / 64;  // 1024 B per tile
         const int in_tile = (int)(i % 64);
         const int lane = in_tile >> 1, half = in_tile & 1;
         const int g = lane >> 2, t = lane & 3;
-        const int64_t r_dev = tp.rb * 16 + g + (half ? 8 : 0);
-        const int64_t col = tp.c * 64 + 16 * t;
-        uint4* dst = out + tp.dst * 64 + in_tile;
+        const int64_t rb = tile / C, c = tile % C;
+        const int64_t r_dev = rb * 16 + g + (half ? 8 : 0);
+        const int64_t col = c * 64 + 16 * t;
+        uint4* dst = out + ((rb0 + rb) * C + c) * 64 + in_tile;
         if (!unpack) {
-            if (tp.c < C) {
-                int which;
-                const int64_t r = src_row(r_dev, il, which);
-                *dst = *reinterpret_cast<const uint4*>((which ? b : a) + r * K + col);
-            } else {
-                *dst = make_uint4(0, 0, 0, 0);
-            }
-        } else if (tp.c < C) {
+            int which;
+            const int64_t r = src_row(r_dev, il, which);
+            *dst = *reinterpret_cast<const uint4*>((which ? b : a) + r * K + col);
+        } else {
             *reinterpret_cast<uint4*>(const_cast<int8_t*>(a) + r_dev * K + col) = *dst;
         }
     }
@@ -634,6 +719,7 @@ am_status_code prepack_impl(int32_t format, int32_t dtype, int64_t n, int64_t k,
                             int64_t row0, const void* qa, const void* sa, const void* qb, const void* sb, bool il,
                             void* qp, void* sp, cudaStream_t s) {
     (void)group;
+    (void)n_total;
     if (format == AMCU_WFMT_PLAIN) {
         uint8_t* dst = static_cast<uint8_t*>(qp) + row0 * k * plain_elt(dtype);
         if (!il) {
@@ -642,23 +728,14 @@ am_status_code prepack_impl(int32_t format, int32_t dtype, int64_t n, int64_t k,
             const int64_t hb = n / 2 * k * plain_elt(dtype);
             copy_bytes_kernel<<<pack_grid(2 * hb), 256, 0, s>>>((const uint8_t*)qa, (const uint8_t*)qb, hb, dst);
         }
-        return check_launch("amcu_prepack_weight");
-    }
-    const StreamGeom sg = stream_geom(k);
-    const PackGeom pg{n / 16, n_total / 16, row0 / 16, sg.kc, sg.tw};
-    const int64_t stream_tiles = (int64_t)sg.kc * (n_total / 16) * sg.tw;
-    const int64_t part_tiles = (int64_t)sg.kc * (n / 16) * sg.tw;
-    if (format == AMCU_WFMT_INT4) {
-        pack_w4_kernel<<<pack_grid(part_tiles * 128), 256, 0, s>>>((const uint8_t*)qa, (const uint8_t*)qb, il, k, pg,
-                                                                   (uint32_t*)qp, false, nullptr);
-        cudaMemsetAsync(static_cast<uint8_t*>(qp) + stream_tiles * 512, 0, kStreamPadBytes, s);
-        pack_s4_kernel<<<pack_grid(part_tiles / 2 * 16), 256, 0, s>>>((const __half*)sa, (const __half*)sb, il,
-                                                                      k / 128, pg, (__half*)sp, false);
-        cudaMemsetAsync(static_cast<uint8_t*>(sp) + stream_tiles / 2 * 32, 0, kScalePadBytes, s);
+    } else if (format == AMCU_WFMT_INT4) {
+        const int64_t words = n / 16 * (k / 128) * (kW4PairBytes / 4);
+        pack_w4_kernel<<<pack_grid(words), 256, 0, s>>>((const uint8_t*)qa, (const uint8_t*)qb, (const __half*)sa,
+                                                        (const __half*)sb, il, n, k, row0 / 16, (uint32_t*)qp, false,
+                                                        nullptr, nullptr);
     } else {
-        pack_w8_kernel<<<pack_grid(part_tiles * 64), 256, 0, s>>>((const int8_t*)qa, (const int8_t*)qb, il, k, pg,
-                                                                  (uint4*)qp, false);
-        cudaMemsetAsync(static_cast<uint8_t*>(qp) + stream_tiles * 1024, 0, kStreamPadBytes, s);
+        pack_w8_kernel<<<pack_grid(n * k / 16), 256, 0, s>>>((const int8_t*)qa, (const int8_t*)qb, il, n, k, row0 / 16,
+                                                            (uint4*)qp, false);
         pack_s8_kernel<<<pack_grid(n), 256, 0, s>>>((const float*)sa, (const float*)sb, il, n,
                                                     static_cast<float*>(sp) + row0);
     }
@@ -671,19 +748,15 @@ extern "C" {
 int64_t amcu_packed_weight_bytes(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group) {
     (void)group;
     if (format == AMCU_WFMT_PLAIN) return n * k * plain_elt(dtype);
-    const StreamGeom sg = stream_geom(k);
-    const int64_t tiles = (int64_t)sg.kc * (n / 16) * sg.tw;
-    return tiles * (format == AMCU_WFMT_INT8 ? 1024 : 512) + kStreamPadBytes;
+    if (format == AMCU_WFMT_INT8) return n * k;
+    return n / 16 * (k / 128) * kW4PairBytes;  // weights and scales together
 }
 
 int64_t amcu_packed_scale_bytes(int32_t format, int64_t n, int64_t k, int64_t group) {
+    (void)k;
     (void)group;
     if (format == AMCU_WFMT_INT8) return n * 4;
-    if (format == AMCU_WFMT_INT4) {
-        const StreamGeom sg = stream_geom(k);
-        return (int64_t)sg.kc * (n / 16) * (sg.tw / 2) * 32 + kScalePadBytes;
-    }
-    return 0;
+    return 0;  // INT4 scales live inside the packed weight
 }
 
 am_status_code amcu_prepack_weight(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group,
@@ -692,7 +765,8 @@ am_status_code amcu_prepack_weight(int32_t format, int32_t dtype, int64_t n, int
     am_status_code st = check_weight_shape(format, dtype, n, k, group);
     if (st != AM_STATUS_OK) return st;
     AMCU_REQUIRE(q && qp, "amcu_prepack_weight: null pointer");
-    AMCU_REQUIRE(format == AMCU_WFMT_PLAIN || (sc && sp), "amcu_prepack_weight: null scale pointer");
+    AMCU_REQUIRE(format == AMCU_WFMT_PLAIN || sc, "amcu_prepack_weight: null scale pointer");
+    AMCU_REQUIRE(format != AMCU_WFMT_INT8 || sp, "amcu_prepack_weight: null packed scale pointer");
     AMCU_REQUIRE(aligned(qp, 16) && aligned(q, 16), "amcu_prepack_weight: weights must be 16-byte aligned");
     return prepack_impl(format, dtype, n, k, group, n, 0, q, sc, q, sc, false, qp, sp, as_stream(stream));
 }
@@ -709,7 +783,8 @@ am_status_code amcu_prepack_weight_rows(int32_t format, int32_t dtype, int64_t n
                  "amcu_prepack_weight_rows: rows [%lld, %lld) must lie in [0, %lld) and start on a 16-row boundary",
                  (long long)row0, (long long)(row0 + n), (long long)n_total);
     AMCU_REQUIRE(q && qp, "amcu_prepack_weight_rows: null pointer");
-    AMCU_REQUIRE(format == AMCU_WFMT_PLAIN || (sc && sp), "amcu_prepack_weight_rows: null scale pointer");
+    AMCU_REQUIRE(format == AMCU_WFMT_PLAIN || sc, "amcu_prepack_weight_rows: null scale pointer");
+    AMCU_REQUIRE(format != AMCU_WFMT_INT8 || sp, "amcu_prepack_weight_rows: null packed scale pointer");
     AMCU_REQUIRE(aligned(qp, 16) && aligned(q, 16), "amcu_prepack_weight_rows: weights must be 16-byte aligned");
     return prepack_impl(format, dtype, n, k, group, n_total, row0, q, sc, q, sc, false, qp, sp, as_stream(stream));
 }
@@ -722,7 +797,8 @@ am_status_code amcu_prepack_gate_up(int32_t format, int32_t dtype, int64_t inter
     am_status_code st = check_weight_shape(format, dtype, 2 * inter, k, group);
     if (st != AM_STATUS_OK) return st;
     AMCU_REQUIRE(gq && uq && qp, "amcu_prepack_gate_up: null pointer");
-    AMCU_REQUIRE(format == AMCU_WFMT_PLAIN || (gs && us && sp), "amcu_prepack_gate_up: null scale pointer");
+    AMCU_REQUIRE(format == AMCU_WFMT_PLAIN || (gs && us), "amcu_prepack_gate_up: null scale pointer");
+    AMCU_REQUIRE(format != AMCU_WFMT_INT8 || sp, "amcu_prepack_gate_up: null packed scale pointer");
     AMCU_REQUIRE(aligned(qp, 16) && aligned(gq, 16) && aligned(uq, 16), "amcu_prepack_gate_up: misaligned");
     return prepack_impl(format, dtype, 2 * inter, k, group, 2 * inter, 0, gq, gs, uq, us, true, qp, sp,
                         as_stream(stream));
@@ -737,20 +813,14 @@ am_status_code amcu_unpack_weight(int32_t format, int32_t dtype, int64_t n, int6
     cudaStream_t s = as_stream(stream);
     if (format == AMCU_WFMT_PLAIN) {
         cudaMemcpyAsync(q, qp, (size_t)n * k * plain_elt(dtype), cudaMemcpyDeviceToDevice, s);
-        return check_launch("amcu_unpack_weight");
-    }
-    const StreamGeom sg = stream_geom(k);
-    const PackGeom pg{n / 16, n / 16, 0, sg.kc, sg.tw};
-    const int64_t tiles = (int64_t)sg.kc * (n / 16) * sg.tw;
-    if (format == AMCU_WFMT_INT4) {
-        pack_w4_kernel<<<pack_grid(tiles * 128), 256, 0, s>>>(nullptr, nullptr, false, k, pg,
-                                                              (uint32_t*)const_cast<void*>(qp), true, (uint8_t*)q);
-        if (sc && sp)
-            pack_s4_kernel<<<pack_grid(tiles / 2 * 16), 256, 0, s>>>((const __half*)sc, nullptr, false, k / 128, pg,
-                                                                     (__half*)const_cast<void*>(sp), true);
+    } else if (format == AMCU_WFMT_INT4) {
+        (void)sp;
+        pack_w4_kernel<<<pack_grid(n / 16 * (k / 128) * (kW4PairBytes / 4)), 256, 0, s>>>(
+                nullptr, nullptr, nullptr, nullptr, false, n, k, 0, (uint32_t*)const_cast<void*>(qp), true,
+                (uint8_t*)q, (__half*)sc);
     } else {
-        pack_w8_kernel<<<pack_grid(tiles * 64), 256, 0, s>>>((const int8_t*)q, nullptr, false, k, pg,
-                                                             (uint4*)const_cast<void*>(qp), true);
+        pack_w8_kernel<<<pack_grid(n * k / 16), 256, 0, s>>>((const int8_t*)q, nullptr, false, n, k, 0,
+                                                            (uint4*)const_cast<void*>(qp), true);
         if (sc && sp) cudaMemcpyAsync(sc, sp, (size_t)n * 4, cudaMemcpyDeviceToDevice, s);
     }
     return check_launch("amcu_unpack_weight");

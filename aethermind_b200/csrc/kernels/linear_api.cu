@@ -27,7 +27,7 @@ am_status_code validate_linear(const AmcuLinearArgs* a, const char* who) {
     } else {
         AMCU_REQUIRE(w.format == AMCU_WFMT_INT8 || w.format == AMCU_WFMT_INT4, "%s: unknown weight format", who);
         AMCU_REQUIRE(a->act_dtype == AMCU_BF16, "%s: quantized weights take bf16 activations", who);
-        AMCU_REQUIRE(w.scales, "%s: null scales", who);
+        AMCU_REQUIRE(w.format != AMCU_WFMT_INT8 || w.scales, "%s: null scales", who);
         AMCU_REQUIRE(w.n % 16 == 0 && w.k % 64 == 0, "%s: n %% 16 and k %% 64 must be 0", who);
         AMCU_REQUIRE(w.format != AMCU_WFMT_INT4 || (w.group == 128 && w.k % 128 == 0),
                      "%s: int4 needs group 128 and k %% 128 == 0", who);
@@ -53,6 +53,7 @@ GemvParams make_params(const AmcuLinearArgs* a) {
     p.err = device_error_word();
     p.norm_w = a->norm_weight;
     p.eps = a->norm_eps;
+    p.l2_next = a->l2_next;
     return p;
 }
 

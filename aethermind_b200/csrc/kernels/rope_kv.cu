@@ -13,13 +13,6 @@
 
 namespace amcu {
 
-__device__ __forceinline__ void rope_angle(double theta, int64_t d, int64_t pos, int64_t i, float& c, float& s) {
-    const double inv = 1.0 / pow(theta, 2.0 * (double)i / (double)d);
-    const double ang = (double)pos * inv;
-    c = (float)cos(ang);
-    s = (float)sin(ang);
-}
-
 __global__ void rope_table_kernel(double theta, int64_t d, int64_t max_pos, float2* table) {
     const int64_t half = d / 2;
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < max_pos * half;

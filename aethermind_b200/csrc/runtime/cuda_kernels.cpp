@@ -7,6 +7,8 @@
 //   Add + RMSNorm          -> kRmsNorm with a residual input
 //   q/k/v Linear           -> one kLinear over the concatenated [q;k;v] weight
 //   RoPE + KVCacheUpdate   -> kRoPE (rotates q, writes rotated k and v to the cache)
+//   RoPE + KVCacheUpdate + Attention (decode, bf16)
+//                          -> kRoPEAttention (one launch, rotated q stays on chip)
 //   o Linear + Add         -> kLinear with the residual-add epilogue
 //   gate/up Linear+SiluMul -> kLinear over the interleaved gate/up weight (SiLU-Mul epilogue)
 //   down Linear + Add      -> kLinear with the residual-add epilogue
@@ -183,6 +185,64 @@ Status AttnPrefillFn(const KernelContext& c) noexcept {
     return FromAm(amcu_attn_prefill(&a, S(c)));
 }
 
+// ---- fused decode RoPE + KV append + attention ----
+struct RopeAttnArgs {
+    AmcuRopeKvArgs rope;
+    AmcuAttentionArgs attn;
+};
+// in: (q, k, v, k_cache, v_cache); out: (o, k_cache, v_cache)
+Status BuildRopeAttention(std::span<const TensorView> in, std::span<const MutableTensorView> out,
+                          std::span<const std::byte> attrs, const void*, void* buf) noexcept {
+    if (in.size() < 5 || out.size() < 3)
+        return Status::InvalidArgument("RoPEAttention expects (q, k, v, k_cache, v_cache) -> (o, k_cache, v_cache)");
+    const auto* at = Attrs<RopeAttentionAttrs>(attrs);
+    if (!at) return Status::InvalidArgument("RoPEAttention attrs missing");
+    auto* a = new (buf) RopeAttnArgs{};
+    AmcuRopeKvArgs& r = a->rope;
+    r.q = const_cast<void*>(in[0].data);
+    r.k = in[1].data;
+    r.v = in[2].data;
+    r.q_stride = in[0].strides[0];
+    r.k_stride = in[1].strides[0];
+    r.v_stride = in[2].strides[0];
+    r.k_cache = out[1].mutable_data();
+    r.v_cache = out[2].mutable_data();
+    r.slot_stride = at->rope.slot_stride;
+    r.capacity = at->rope.capacity;
+    r.seq_pos = at->rope.seq_pos;
+    r.rows = in[0].dim(0);
+    r.rows_per_seq = at->rope.rows_per_seq;
+    r.n_q_heads = at->rope.n_q;
+    r.n_kv_heads = at->rope.n_kv;
+    r.head_dim = at->rope.head_dim;
+    r.theta = at->rope.theta;
+    r.dtype = AmDtype(in[0].dtype);
+    r.status = at->rope.status;
+    r.cos_sin = at->rope.cos_sin;
+    AmcuAttentionArgs& t = a->attn;
+    t.q = in[0].data;
+    t.q_stride = in[0].strides[0];
+    t.k_cache = out[1].mutable_data();
+    t.v_cache = out[2].mutable_data();
+    t.slot_stride = at->attn.slot_stride;
+    t.capacity = at->attn.capacity;
+    t.seq_pos = at->attn.seq_pos;
+    t.out = out[0].mutable_data();
+    t.out_stride = out[0].strides[0];
+    t.rows = in[0].dim(0);
+    t.rows_per_seq = at->attn.rows_per_seq;
+    t.n_q_heads = at->attn.n_q;
+    t.n_kv_heads = at->attn.n_kv;
+    t.head_dim = at->attn.head_dim;
+    t.dtype = AmDtype(in[0].dtype);
+    t.max_context = at->attn.max_context;
+    return Status::Ok();
+}
+Status RopeAttnFn(const KernelContext& c) noexcept {
+    const auto* a = static_cast<const RopeAttnArgs*>(c.kernel_params);
+    return FromAm(amcu_attn_decode_rope(&a->rope, &a->attn, S(c)));
+}
+
 // ---- elementwise ----
 struct BinaryArgs {
     const void* a;
@@ -303,6 +363,10 @@ AM_REGISTER_KERNEL(Attn_CUDA_F32_Prefill, KernelDescriptor{OpType::kAttention, A
 AM_REGISTER_KERNEL(Attn_CUDA_BF16_Prefill, KernelDescriptor{OpType::kAttention, AM_SEL(kBF16, kBF16, kPlain, kPrefill),
                                                             AttnPrefillFn, "AttnPrefill_CUDA_BF16", 0, BuildAttention,
                                                             sizeof(AmcuAttentionArgs)})
+
+AM_REGISTER_KERNEL(RoPEAttn_CUDA_BF16_Decode,
+                   KernelDescriptor{OpType::kRoPEAttention, AM_SEL(kBF16, kBF16, kPlain, kDecode), RopeAttnFn,
+                                    "RoPEAttnDecodeCluster_CUDA_BF16", 0, BuildRopeAttention, sizeof(RopeAttnArgs)})
 
 AM_REGISTER_KERNEL(SiluMul_CUDA_F32, KernelDescriptor{OpType::kSiluMul, AM_SEL(kF32, kF32, kPlain, kBoth), SiluMulFn,
                                                       "SiluMul_CUDA_F32", 0, BuildBinary, sizeof(BinaryArgs)})

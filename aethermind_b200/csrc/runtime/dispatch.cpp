@@ -34,6 +34,7 @@ const char* ToString(OpType op) noexcept {
         case OpType::kReshape: return "Reshape";
         case OpType::kPermute: return "Permute";
         case OpType::kReorder: return "Reorder";
+        case OpType::kRoPEAttention: return "RoPEAttention";
         default: return "Unknown";
     }
 }

@@ -44,6 +44,7 @@ enum class OpType : uint16_t {
     kReshape,
     kPermute,
     kReorder,
+    kRoPEAttention,  // fused decode step: RoPE + KVCacheUpdate + Attention
 };
 const char* ToString(OpType op) noexcept;
 

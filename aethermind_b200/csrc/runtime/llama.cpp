@@ -107,7 +107,7 @@ Status AllocLinear(am_model_s* m, LinearWeight& lw, int64_t n, int64_t k, bool g
     auto q = m->rt->alloc->Allocate(WeightBytes(c, n, k));
     if (!q.ok()) return q.status();
     lw.q = std::move(q.value());
-    if (c.weight_format != AMCU_WFMT_PLAIN) {
+    if (ScaleBytes(c, n, k) > 0) {  // INT8; INT4 scales live inside the packed weight
         auto s = m->rt->alloc->Allocate(ScaleBytes(c, n, k));
         if (!s.ok()) return s.status();
         lw.s = std::move(s.value());
@@ -409,6 +409,40 @@ MutableTensorView MView2(void* p, DType dt, int64_t rows, int64_t cols, int64_t 
     return v;
 }
 
+// Weight prefetch across kernel boundaries: every quantized Linear step asks
+// for the next Linear step's weights and scales to be pulled into L2 while it
+// runs (the last step of the plan asks for the first one's, which the next
+// decode step reads), and for the one after that too when the next weight is
+// small, so HBM keeps streaming through the short kernels in between.
+void SetL2Hints(ExecutionPlan& plan) {
+    constexpr uint64_t kMaxRange = 64ull << 20;   // L2 is 126 MB
+    constexpr uint64_t kSmallWeight = 16ull << 20;
+    std::vector<size_t> lin;
+    for (size_t i = 0; i < plan.steps.size(); ++i) {
+        const auto* w = static_cast<const AmcuWeight*>(plan.steps[i].packed_weights);
+        if (plan.steps[i].op == OpType::kLinear && w && w->format != AMCU_WFMT_PLAIN) lin.push_back(i);
+    }
+    if (lin.size() < 2) return;
+    auto weight_of = [&](size_t j) { return static_cast<const AmcuWeight*>(plan.steps[lin[j % lin.size()]].packed_weights); };
+    auto wbytes = [](const AmcuWeight* w) {
+        return (uint64_t)amcu_packed_weight_bytes(w->format, w->dtype, w->n, w->k, w->group);
+    };
+    for (size_t j = 0; j < lin.size(); ++j) {
+        AmcuL2Prefetch h{};
+        int slot = 0;
+        for (size_t ahead = 1; ahead <= 2 && slot + 2 <= 4; ++ahead) {
+            const AmcuWeight* w = weight_of(j + ahead);
+            const uint64_t b = wbytes(w);
+            h.ptr[slot] = w->data;
+            h.bytes[slot++] = b < kMaxRange ? b : kMaxRange;
+            h.ptr[slot] = w->scales;
+            h.bytes[slot++] = (uint64_t)amcu_packed_scale_bytes(w->format, w->n, w->k, w->group);
+            if (b >= kSmallWeight) break;
+        }
+        reinterpret_cast<AmcuLinearArgs*>(plan.steps[lin[j]].params.data())->l2_next = h;
+    }
+}
+
 Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, ExecutionPlan& plan) {
     am_model_s* m = s->m;
     const auto& c = m->cfg;
@@ -428,6 +462,11 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
     // Decode GEMVs (m <= 8) stage their activations anyway: the RMSNorm in
     // front of q/k/v and gate/up runs there instead of as its own kernel.
     const bool fuse_norm = phase == ExecPhase::kDecode && wf != WeightFormat::kPlain && M <= 8;
+    // decode attention blocks as one fused RoPE + attention launch where a
+    // kernel for it is registered (bf16) and the session does not ask for
+    // the unfused steps
+    const bool fuse_attn = phase == ExecPhase::kDecode && R == B && s->cfg.unfused_attention == 0 &&
+                           m->rt->backend->ResolveKernelInfo(OpType::kRoPEAttention, act).ok();
     s->ar_ctx.clear();
 
     // Embedding
@@ -469,11 +508,23 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
                                                                       (int64_t)s->kv.layout().max_tokens, d});
         MutableTensorView vc = MakeMutableView(s->kv.value_plane(l), A, {(int64_t)s->kv.layout().num_slots, m->nkv_l,
                                                                         (int64_t)s->kv.layout().max_tokens, d});
-        AM_RETURN_IF_ERROR(pb.Add(OpType::kRoPE, act, {q, k, v}, {qo, kc, vc}, &ra, nullptr, p + "rope_kv_write", true));
         AttentionAttrs aa{R, (int64_t)s->kv.layout().max_tokens, (int64_t)(s->kv.layout().slot_stride / e), m->nq_l,
                           m->nkv_l, d, c.max_seq, s->seq_pos.as<int32_t>(), 0};
-        AM_RETURN_IF_ERROR(pb.Add(OpType::kAttention, act, {q, kc, vc}, {MView2(s->attn.data(), A, M, qn, qn)}, &aa,
-                                  nullptr, p + "attention", true));
+        if (fuse_attn) {  // RoPE + KV append + attention in one launch
+            RopeAttentionAttrs fa{ra, aa};
+            TensorView kcv = MakeView(kc.data, A, {(int64_t)s->kv.layout().num_slots, m->nkv_l,
+                                                   (int64_t)s->kv.layout().max_tokens, d});
+            TensorView vcv = MakeView(vc.data, A, {(int64_t)s->kv.layout().num_slots, m->nkv_l,
+                                                   (int64_t)s->kv.layout().max_tokens, d});
+            AM_RETURN_IF_ERROR(pb.Add(OpType::kRoPEAttention, act, {q, k, v, kcv, vcv},
+                                      {MView2(s->attn.data(), A, M, qn, qn), kc, vc}, &fa, nullptr,
+                                      p + "rope_kv_write+attention", true));
+        } else {
+            AM_RETURN_IF_ERROR(
+                    pb.Add(OpType::kRoPE, act, {q, k, v}, {qo, kc, vc}, &ra, nullptr, p + "rope_kv_write", true));
+            AM_RETURN_IF_ERROR(pb.Add(OpType::kAttention, act, {q, kc, vc}, {MView2(s->attn.data(), A, M, qn, qn)},
+                                      &aa, nullptr, p + "attention", true));
+        }
         auto residual_block = [&](LinearWeight& W, const TensorView& in, const std::string& name) -> Status {
             if (!tp) {
                 LinearAttrs res{AMCU_EPI_RESIDUAL_ADD};
@@ -519,6 +570,7 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
     ArgmaxAttrs ga{s->gap_tmp.as<float>()};
     AM_RETURN_IF_ERROR(pb.Add(OpType::kArgmax, act, {View2(s->logits.data(), A, B, c.vocab, c.vocab)},
                               {MakeMutableView(s->next_tok.data(), DType::kI64, {B})}, &ga, nullptr, "argmax"));
+    SetL2Hints(plan);
     return Status::Ok();
 }
 

@@ -25,6 +25,10 @@ struct AttentionAttrs {
     const int32_t* seq_pos;
     int32_t num_splits;
 };
+struct RopeAttentionAttrs {
+    RopeKvAttrs rope;
+    AttentionAttrs attn;
+};
 struct EmbeddingAttrs {
     const float* row_scales;
     int32_t* status;

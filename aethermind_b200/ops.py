@@ -236,6 +236,41 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq
     return o
 
 
+def attention_rope_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor,
+                          v_cache: torch.Tensor, seq_pos: torch.Tensor, n_q: int, n_kv: int, head_dim: int,
+                          theta: float, cos_sin: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                          out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused decode step (amcu_attn_decode_rope): RoPE, KV-cache append and
+    attention for one row per sequence. q is not modified."""
+    _require_cuda(q, k, v, k_cache, v_cache, seq_pos)
+    rows = q.shape[0]
+    o = out if out is not None else torch.empty(rows, n_q * head_dim, dtype=q.dtype, device=q.device)
+    r = L.AmcuRopeKvArgs()
+    r.q, r.k, r.v = _p(q), _p(k), _p(v)
+    r.q_stride, r.k_stride, r.v_stride = q.stride(0), k.stride(0), v.stride(0)
+    r.k_cache, r.v_cache = _p(k_cache), _p(v_cache)
+    r.slot_stride, r.capacity = k_cache.stride(0), k_cache.shape[2]
+    r.seq_pos = _p(seq_pos)
+    r.rows, r.rows_per_seq = rows, 1
+    r.n_q_heads, r.n_kv_heads, r.head_dim = n_q, n_kv, head_dim
+    r.theta = theta
+    r.dtype = _dt(q)
+    r.status = _p(status)
+    r.cos_sin = _p(cos_sin)
+    a = L.AmcuAttentionArgs()
+    a.q, a.q_stride = _p(q), q.stride(0)
+    a.k_cache, a.v_cache = _p(k_cache), _p(v_cache)
+    a.slot_stride, a.capacity = k_cache.stride(0), k_cache.shape[2]
+    a.seq_pos = _p(seq_pos)
+    a.out, a.out_stride = _p(o), o.stride(0)
+    a.rows, a.rows_per_seq = rows, 1
+    a.n_q_heads, a.n_kv_heads, a.head_dim = n_q, n_kv, head_dim
+    a.dtype = _dt(q)
+    a.max_context = k_cache.shape[2]
+    check(lib().amcu_attn_decode_rope(C.byref(r), C.byref(a), _stream()), "amcu_attn_decode_rope")
+    return o
+
+
 def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     _require_cuda(gate, up)
     y = out if out is not None else torch.empty_like(gate)

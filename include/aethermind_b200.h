@@ -113,11 +113,12 @@ typedef struct AmcuWeight {
     int64_t k;            /* input features */
     int64_t group;        /* INT4 group size along K (128); ignored otherwise */
     const void* data;     /* device-format weights */
-    const void* scales;   /* device-format scales (INT8/INT4) */
+    const void* scales;   /* device-format scales (INT8; INT4 keeps them inside `data`, may be NULL) */
     int32_t gate_up_interleaved; /* 1: rows are [gate;up] interleaved by amcu_prepack_gate_up */
 } AmcuWeight;
 
-/* Bytes of the device-format weight / scale buffers. */
+/* Bytes of the device-format weight / scale buffers (INT4: the scales are
+ * part of the weight buffer and the scale buffer size is 0). */
 int64_t amcu_packed_weight_bytes(int32_t format, int32_t dtype, int64_t n, int64_t k, int64_t group);
 int64_t amcu_packed_scale_bytes(int32_t format, int64_t n, int64_t k, int64_t group);
 /* canonical (device pointers) -> device format. */
@@ -191,6 +192,19 @@ typedef enum amcu_epilogue {
     AMCU_EPI_SILU_MUL = 2      /* gate/up interleaved weight: y[m, i] = round(silu(round(g)) * round(u)) */
 } amcu_epilogue;
 
+/* Optional L2 prefetch hint: up to four byte ranges that the NEXT operation
+ * on the stream will read (its weights and scales). The kernel asks the TMA
+ * engine to pull them into L2 while it runs, spread over its CTAs, so the
+ * next kernel finds its weights in L2 and HBM stays busy across kernel
+ * boundaries. Pointers 16-byte aligned; sizes are rounded down to multiples
+ * of 16; a NULL pointer or zero size is an unused slot. A hint never changes
+ * results. (No counterpart in the reference, whose CPU kernels have no
+ * device cache to fill.) */
+typedef struct AmcuL2Prefetch {
+    const void* ptr[4];
+    uint64_t bytes[4];
+} AmcuL2Prefetch;
+
 typedef struct AmcuLinearArgs {
     const void* x;          /* [m, k] act dtype, row stride x_stride */
     AmcuWeight w;
@@ -206,6 +220,7 @@ typedef struct AmcuLinearArgs {
     const void* norm_weight; /* optional: x is first RMS-normalized with this [k] weight
                                 (the RMSNorm that precedes q/k/v and gate/up, fused) */
     float norm_eps;
+    AmcuL2Prefetch l2_next;  /* optional: ranges the next operation reads */
 } AmcuLinearArgs;
 /* Dispatches on m: GEMV (m <= 8) or the tensor-core GEMM (m > 8). */
 am_status_code amcu_linear(const AmcuLinearArgs* args, void* stream);
@@ -280,6 +295,13 @@ typedef struct AmcuAttentionArgs {
 } AmcuAttentionArgs;
 size_t amcu_attention_workspace_bytes(const AmcuAttentionArgs* args);
 am_status_code amcu_attn_decode(const AmcuAttentionArgs* args, void* stream);
+/* Fused decode step: amcu_rope_kv_write(rope) then amcu_attn_decode(attn) in
+ * one launch (bf16, one row per sequence; attn->q == rope->q, same caches and
+ * positions). The rotated q is used on chip and NOT written back to rope->q;
+ * the rotated k and v of the token are appended to the cache as
+ * amcu_rope_kv_write does. No workspace: the split-K partials are merged
+ * through distributed shared memory of a thread-block cluster. */
+am_status_code amcu_attn_decode_rope(const AmcuRopeKvArgs* rope, const AmcuAttentionArgs* attn, void* stream);
 am_status_code amcu_attn_prefill(const AmcuAttentionArgs* args, void* stream);
 /* Decode attention that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory while they run: a server
@@ -370,6 +392,8 @@ typedef struct am_model_config_t {
 typedef struct am_session_config_t {
     int64_t max_new_tokens;
     int32_t use_cuda_graph;  /* 1: decode steps replay a captured CUDA graph */
+    int32_t unfused_attention; /* 1: decode RoPE and attention as two launches (default 0: one fused
+                                  launch, amcu_attn_decode_rope, where the dtype has one) */
 } am_session_config_t;
 
 am_runtime_t am_runtime_create(const am_config_t* config);

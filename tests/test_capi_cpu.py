@@ -103,13 +103,11 @@ def test_argument_validation_without_gpu(built_lib):
     la.act_dtype = L.BF16
     la.w.group = 128
     assert built_lib.amcu_linear(C.byref(la), None) == 3  # k % 64 != 0
-    # K-chunked stream: no padding tiles for K = 4096, plus the fixed tail slack
-    assert built_lib.amcu_packed_weight_bytes(L.WFMT_INT4, L.BF16, 4096, 4096, 128) == 4096 * 2048 + 16384
-    assert built_lib.amcu_packed_scale_bytes(L.WFMT_INT4, 4096, 4096, 128) == 4096 * 32 * 2 + 256
-    # K = 1792 (28 tiles) packs as 7 chunks of 4 tiles: no padding either
-    assert built_lib.amcu_packed_weight_bytes(L.WFMT_INT8, L.BF16, 64, 1792, 128) == 64 * 1792 + 16384
-    # K = 384 (6 tiles) pads to 2 chunks of 4 tiles
-    assert built_lib.amcu_packed_weight_bytes(L.WFMT_INT4, L.BF16, 16, 384, 128) == 8 * 512 + 16384
+    # INT4 pair records carry the group scales: 2 x 512 B of nibbles + 32 B of fp16 scales per 16 x 128
+    assert built_lib.amcu_packed_weight_bytes(L.WFMT_INT4, L.BF16, 4096, 4096, 128) == 4096 * 2048 + 4096 * 32 * 2
+    assert built_lib.amcu_packed_scale_bytes(L.WFMT_INT4, 4096, 4096, 128) == 0
+    assert built_lib.amcu_packed_weight_bytes(L.WFMT_INT8, L.BF16, 64, 1792, 128) == 64 * 1792
+    assert built_lib.amcu_packed_scale_bytes(L.WFMT_INT8, 64, 1792, 128) == 64 * 4
     err = C.c_void_p()
     assert built_lib.am_model_load(None, b"/nonexistent", C.byref(err)) is None
     assert built_lib.am_error_code(err) == 12

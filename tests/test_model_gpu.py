@@ -70,6 +70,9 @@ def test_quantized_model_matches_oracle(sess_mod, rt, oracle_lib, cfg_name):
     ref, gaps = om.generate(prompt.astype(np.int64), 8)
     n = _compare(got.tolist(), ref.tolist(), gaps, 0.125)
     assert n >= 4
+    # the unfused RoPE + attention steps give the same tokens
+    s_unfused = sess_mod.Session(m, fused_attention=False)
+    np.testing.assert_array_equal(s_unfused.generate(prompt, 8), got)
     # batch of 2 equals two single runs (per-row math is independent of the batch)
     p2 = np.stack([prompt, np.random.default_rng(6).integers(0, cfg.vocab, 16).astype(np.uint32)])
     gb = s.generate(p2, 8)
@@ -85,7 +88,9 @@ def test_plan_resolves_phase_kernels(sess_mod, rt):
     dec = s.plan_steps(1, 1, 1)
     pre = s.plan_steps(0, 1, 16)
     assert any("GemvW4G128_CUDA_Decode" in l for l in dec)
-    assert any("AttnDecodeSplitK" in l for l in dec)
+    assert any("RoPEAttnDecodeCluster_CUDA_BF16" in l for l in dec)
+    unf = sess_mod.Session(m, fused_attention=False).plan_steps(1, 1, 1)
+    assert any("AttnDecodeSplitK" in l for l in unf)
     assert any("GemmW4G128_CUDA_Prefill" in l for l in pre)
     assert any("AttnPrefill" in l for l in pre)
     names = [l.split()[0] for l in dec]

@@ -61,7 +61,7 @@ def test_synth_bit_exact_vs_oracle(ops, orc):
 
 
 @pytest.mark.parametrize("fmt", ["int4", "int8"])
-@pytest.mark.parametrize("k", [1024, 384, 1792])  # 8 chunks; 2 chunks with padding tiles; 7 chunks
+@pytest.mark.parametrize("k", [1024, 384, 1792])
 def test_prepack_roundtrip_bit_exact(ops, fmt, k):
     from aethermind_b200 import _lib as L
     n = 96
@@ -90,18 +90,20 @@ def test_prepack_rows_builds_fused_weight(ops, fmt):
     whole = ops.prepack(f, torch.cat(qs), torch.cat(ss), n_total, k)
     fused = ops.prepack(f, torch.cat(qs), torch.cat(ss), n_total, k)
     fused.data.zero_()
-    fused.scales.zero_()
+    if fused.scales is not None:
+        fused.scales.zero_()
     row0 = 0
     for q, s, n in zip(qs, ss, parts):
         code = L.lib().amcu_prepack_weight_rows(f, L.BF16, n, k, 128, n_total, row0, q.data_ptr(), s.data_ptr(),
-                                                fused.data.data_ptr(), fused.scales.data_ptr(),
+                                                fused.data.data_ptr(), ops._p(fused.scales),
                                                 torch.cuda.current_stream().cuda_stream)
         L.check(code, "amcu_prepack_weight_rows")
         row0 += n
     torch.cuda.synchronize()
-    assert torch.equal(fused.data, whole.data) and torch.equal(fused.scales, whole.scales)
+    assert torch.equal(fused.data, whole.data)
+    assert fused.scales is None or torch.equal(fused.scales, whole.scales)
     bad = L.lib().amcu_prepack_weight_rows(f, L.BF16, 32, k, 128, n_total, 8, qs[1].data_ptr(), ss[1].data_ptr(),
-                                           fused.data.data_ptr(), fused.scales.data_ptr(), None)
+                                           fused.data.data_ptr(), ops._p(fused.scales), None)
     assert bad == 3 and b"16-row" in L.lib().amcu_last_error()
 
 
@@ -163,8 +165,7 @@ def test_gemv_matches_oracle(ops, orc, fmt, m, n):
 @pytest.mark.parametrize("m", [1, 3])
 @pytest.mark.parametrize("k", [384, 1792, 14336])
 def test_gemv_stream_geometries(ops, orc, fmt, m, k):
-    """K values whose stream layout pads tiles (384), uses 7 chunks (1792) or
-    long chunks (14336)."""
+    """K values with stages of 3 (384), 14 (1792) and 16 (14336) pair records."""
     n = 48
     pw, host = _w(ops, orc, fmt, n, k, seed=k)
     x = orc.bf16_round(np.random.default_rng(k + m).normal(0, 1, (m, k)).astype(np.float32))
@@ -324,6 +325,53 @@ def test_attention_prefill_causal(ops, orc, dtype):
 
 
 # ------------------------------------------------------------- elementwise
+@pytest.mark.parametrize("nq,nkv,d", [(32, 8, 128), (32, 8, 64), (16, 8, 128), (8, 8, 64)])
+def test_fused_rope_attention_matches_two_step_path(ops, orc, nq, nkv, d):
+    """amcu_attn_decode_rope == amcu_rope_kv_write + amcu_attn_decode: same
+    appended cache rows (bit-exact) and the same outputs within bf16 rounding;
+    ragged positions across sequences, including position 0 and the last
+    cache slot."""
+    cap, B = 1024, 4
+    rng = np.random.default_rng(nq + d)
+    pos = np.array([0, 37, 700, cap - 1], np.int32)
+    qkv = bf16_dev(rng.normal(0, 1, (B, (nq + 2 * nkv) * d)).astype(np.float32))
+    kc = bf16_dev(rng.normal(0, 1, (B, nkv, cap, d)).astype(np.float32))
+    vc = bf16_dev(rng.normal(0, 1, (B, nkv, cap, d)).astype(np.float32))
+    q, k, v = qkv[:, :nq * d], qkv[:, nq * d:(nq + nkv) * d], qkv[:, (nq + nkv) * d:]
+    sp = dev(pos)
+    table = torch.empty(cap * d // 2 * 2, dtype=torch.float32, device="cuda")
+    from aethermind_b200 import _lib as L
+    L.check(L.lib().amcu_rope_table(500000.0, d, cap, table.data_ptr(), torch.cuda.current_stream().cuda_stream),
+            "amcu_rope_table")
+    kc2, vc2, q2 = kc.clone(), vc.clone(), q.clone()
+    fused = ops.attention_rope_decode(q, k, v, kc, vc, sp, nq, nkv, d, 500000.0, cos_sin=table)
+    ops.rope_kv_write(q2, k, v, kc2, vc2, sp, 1, nq, nkv, d, 500000.0)
+    ref = ops.attention(q2, kc2, vc2, sp, 1, nq, nkv, d, max_context=cap)
+    torch.cuda.synchronize()
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    assert torch.equal(q, qkv[:, :nq * d])  # q untouched
+    np.testing.assert_allclose(to_np(fused), to_np(ref), rtol=BF_RTOL, atol=BF_ATOL)
+    # and against the oracle for one sequence
+    b = 2
+    qr = to_np(q2)[b:b + 1]
+    ro = orc.attention(qr, to_np(kc2)[b], to_np(vc2)[b], int(pos[b]), nq, nkv, d, bf=True)
+    np.testing.assert_allclose(to_np(fused)[b:b + 1], ro, rtol=BF_RTOL, atol=BF_ATOL)
+
+
+def test_fused_rope_attention_out_of_range_sets_status(ops):
+    nq, nkv, d, cap = 8, 2, 64, 64
+    q = torch.zeros(1, nq * d, dtype=torch.bfloat16, device="cuda")
+    kv = torch.zeros(1, nkv * d, dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros(1, nkv, cap, d, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.attention_rope_decode(q, kv, kv, kc, vc, torch.tensor([cap], dtype=torch.int32, device="cuda"), nq, nkv, d,
+                              10000.0, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 11  # AM_STATUS_OUT_OF_RANGE
+    assert torch.count_nonzero(kc).item() == 0
+
+
 def test_silu_mul_and_add_match_reference_bits(ops, orc, gold):
     g = torch.from_numpy(gold["silu_g_bf16"].view(np.int16)).cuda().view(torch.bfloat16)
     u = torch.from_numpy(gold["silu_u_bf16"].view(np.int16)).cuda().view(torch.bfloat16)

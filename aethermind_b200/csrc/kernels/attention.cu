@@ -206,13 +206,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(AttnKParams p
     const T* kbase = static_cast<const T*>(p.kc) + b * p.slot_stride + (int64_t)kvh * p.capacity * D;
     const T* vbase = static_cast<const T*>(p.vc) + b * p.slot_stride + (int64_t)kvh * p.capacity * D;
     DecodeWarpState<GRP, D> st;
-    decode_keys_warp<GRP, D>(kbase, vbase, k_begin, k_end, warp, lane, qs, st);
+    decode_keys_warp<GRP, D, kAttnWarps>(kbase, vbase, k_begin, k_end, warp, lane, qs, st);
     decode_publish_warp<GRP, D>(st, warp, lane, sm_m, sm_l, sm_o);
     __syncthreads();
     for (int e = threadIdx.x; e < GRP * D; e += kAttnThreads) {
         const int h = e / D, dd = e % D;
         float M, Ls, O;
-        decode_merge_warps<GRP, D>(h, dd, sm_m, sm_l, sm_o, M, Ls, O);
+        decode_merge_warps<GRP, D, kAttnWarps>(h, dd, sm_m, sm_l, sm_o, M, Ls, O);
         const int64_t qh = (int64_t)kvh * GRP + h;
         if (p.nsplit == 1) {
             T* o = static_cast<T*>(p.out) + row * p.out_stride + qh * D;

@@ -28,6 +28,9 @@ namespace cg = cooperative_groups;
 
 namespace amcu {
 
+constexpr int kRaWarps = 4;  // warps per CTA of the fused kernel
+constexpr int kRaThreads = kRaWarps * 32;
+
 struct RopeAttnParams {
     const __nv_bfloat16 *q, *k, *v;
     int64_t q_stride, k_stride, v_stride;
@@ -42,30 +45,40 @@ struct RopeAttnParams {
     float scale_log2;
 };
 
-template <int GRP, int D>
-__global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(RopeAttnParams p) {
-    pdl_wait();
-    pdl_trigger();
+template <int GRP, int D, int CS>
+__global__ void __launch_bounds__(kRaThreads) attn_rope_decode_kernel(RopeAttnParams p) {
     constexpr int HALF = D / 2;
     cg::cluster_group cluster = cg::this_cluster();
-    const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
+    const int rank = (int)cluster.block_rank();
     const int kvh = blockIdx.y;
     const int64_t row = blockIdx.z;  // one row per sequence
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Before the dependency wait: the position and the cache rows below it
+    // were written by earlier decode steps, which have all completed by the
+    // time this kernel can start (only the preceding q/k/v projection may
+    // still be running).
     const int64_t pos = p.seq_pos[row];
     if (pos < 0 || pos >= p.capacity) {  // the whole cluster leaves together
+        pdl_wait();
         if (rank == 0 && kvh == 0 && threadIdx.x == 0 && p.status) atomicExch(p.status, (int32_t)AM_STATUS_OUT_OF_RANGE);
         return;
     }
     const int64_t L = pos + 1;
-    int64_t chunk = (L + cs - 1) / cs;
+    int64_t chunk = (L + CS - 1) / CS;
     chunk = (chunk + 7) / 8 * 8;
     const int64_t k_begin = (int64_t)rank * chunk;
     const int64_t k_end = k_begin + chunk < L ? k_begin + chunk : L;
+    __nv_bfloat16* kbase = p.kc + row * p.slot_stride + (int64_t)kvh * p.capacity * D;
+    __nv_bfloat16* vbase = p.vc + row * p.slot_stride + (int64_t)kvh * p.capacity * D;
+    DecodeKeyLoop<GRP, D, kRaWarps> loop(kbase, vbase, k_begin, k_end, warp, lane);
+    loop.load_first(pos);  // keys below pos are final
+
+    pdl_wait();
+    pdl_trigger();
 
     __shared__ __align__(16) float qs[GRP][D];
-    __shared__ float sm_m[kAttnWarps][GRP], sm_l[kAttnWarps][GRP];
-    __shared__ float sm_o[kAttnWarps][GRP][D];
+    __shared__ float sm_m[kRaWarps][GRP], sm_l[kRaWarps][GRP];
+    __shared__ float sm_o[kRaWarps][GRP][D];
     __shared__ float pm[GRP], pl[GRP];
     __shared__ float po[GRP][D];
 
@@ -80,7 +93,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(RopeAttn
     };
     // query heads kvh*GRP .. kvh*GRP + GRP - 1, rotated and rounded to bf16
     const __nv_bfloat16* qrow = p.q + row * p.q_stride + (int64_t)kvh * GRP * D;
-    for (int i = threadIdx.x; i < GRP * HALF; i += kAttnThreads) {
+    for (int i = threadIdx.x; i < GRP * HALF; i += kRaThreads) {
         const int h = i / HALF, j = i % HALF;
         float c, s;
         angle(j, c, s);
@@ -90,30 +103,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(RopeAttn
         qs[h][j] = Act<__nv_bfloat16>::round(o1) * p.scale_log2;
         qs[h][j + HALF] = Act<__nv_bfloat16>::round(o2) * p.scale_log2;
     }
-    __nv_bfloat16* kbase = p.kc + row * p.slot_stride + (int64_t)kvh * p.capacity * D;
-    __nv_bfloat16* vbase = p.vc + row * p.slot_stride + (int64_t)kvh * p.capacity * D;
     if (k_begin <= pos && pos < k_end) {  // this CTA's chunk holds the new token: append it
         const __nv_bfloat16* krow = p.k + row * p.k_stride + (int64_t)kvh * D;
         const __nv_bfloat16* vrow = p.v + row * p.v_stride + (int64_t)kvh * D;
-        for (int j = threadIdx.x; j < HALF; j += kAttnThreads) {
+        for (int j = threadIdx.x; j < HALF; j += kRaThreads) {
             float c, s;
             angle(j, c, s);
             const float x1 = __bfloat162float(krow[j]), x2 = __bfloat162float(krow[j + HALF]);
             kbase[pos * D + j] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
             kbase[pos * D + j + HALF] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
         }
-        for (int j = threadIdx.x; j < D; j += kAttnThreads) vbase[pos * D + j] = vrow[j];
+        for (int j = threadIdx.x; j < D; j += kRaThreads) vbase[pos * D + j] = vrow[j];
     }
     __syncthreads();  // q staged; the appended row is visible to this CTA's reads
 
     DecodeWarpState<GRP, D> st;
-    decode_keys_warp<GRP, D>(kbase, vbase, k_begin, k_end, warp, lane, qs, st);
+    loop.run(qs, st);
     decode_publish_warp<GRP, D>(st, warp, lane, sm_m, sm_l, sm_o);
     __syncthreads();
-    for (int e = threadIdx.x; e < GRP * D; e += kAttnThreads) {
+    for (int e = threadIdx.x; e < GRP * D; e += kRaThreads) {
         const int h = e / D, dd = e % D;
         float M, Ls, O;
-        decode_merge_warps<GRP, D>(h, dd, sm_m, sm_l, sm_o, M, Ls, O);
+        decode_merge_warps<GRP, D, kRaWarps>(h, dd, sm_m, sm_l, sm_o, M, Ls, O);
         po[h][dd] = O;
         if (dd == 0) {
             pm[h] = M;
@@ -122,26 +133,38 @@ __global__ void __launch_bounds__(kAttnThreads) attn_rope_decode_kernel(RopeAttn
     }
     cluster.sync();  // every CTA's partial is complete
 
-    for (int e = rank * kAttnThreads + threadIdx.x; e < GRP * D; e += cs * kAttnThreads) {
+    // This CTA combines outputs [rank * per, (rank + 1) * per); all CS
+    // partials of an element are fetched with independent loads.
+    constexpr int per = GRP * D / CS;
+    for (int j = threadIdx.x; j < per; j += kRaThreads) {
+        const int e = rank * per + j;
         const int h = e / D, dd = e % D;
-        float M = -INFINITY;
-        for (int r = 0; r < cs; ++r) M = fmaxf(M, cluster.map_shared_rank(pm, r)[h]);
-        float Ls = 0.f, O = 0.f;
-        for (int r = 0; r < cs; ++r) {
-            const float m = cluster.map_shared_rank(pm, r)[h];
-            if (m == -INFINITY) continue;  // an empty chunk
-            const float f = exp2f(m - M);
-            Ls += cluster.map_shared_rank(pl, r)[h] * f;
-            O += cluster.map_shared_rank(&po[0][0], r)[h * D + dd] * f;
+        float mr[CS], lr[CS], orr[CS];
+#pragma unroll
+        for (int r = 0; r < CS; ++r) {
+            mr[r] = cluster.map_shared_rank(pm, r)[h];
+            lr[r] = cluster.map_shared_rank(pl, r)[h];
+            orr[r] = cluster.map_shared_rank(&po[0][0], r)[e];
         }
-        p.out[row * p.out_stride + ((int64_t)kvh * GRP + h) * D + dd] = __float2bfloat16_rn(O / Ls);
+        float M = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < CS; ++r) M = fmaxf(M, mr[r]);
+        float Ls = 0.f, O = 0.f;
+#pragma unroll
+        for (int r = 0; r < CS; ++r) {
+            const float f = mr[r] == -INFINITY ? 0.f : exp2f(mr[r] - M);  // -inf: an empty chunk
+            Ls += lr[r] * f;
+            O += orr[r] * f;
+        }
+        p.out[row * p.out_stride + (int64_t)kvh * GRP * D + e] = __float2bfloat16_rn(O / Ls);
     }
     cluster.sync();  // partials stay alive until every CTA has read them
 }
 
-template <int GRP, int D>
-static cudaError_t launch_rope_attn(const RopeAttnParams& p, int cs, int64_t nkv, int64_t rows, cudaStream_t s) {
-    auto kern = attn_rope_decode_kernel<GRP, D>;
+template <int GRP, int D, int CS>
+static cudaError_t launch_rope_attn(const RopeAttnParams& p, int64_t nkv, int64_t rows, cudaStream_t s) {
+    constexpr int cs = CS;
+    auto kern = attn_rope_decode_kernel<GRP, D, CS>;
     static bool attr_set = false;
     if (!attr_set) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -149,7 +172,7 @@ static cudaError_t launch_rope_attn(const RopeAttnParams& p, int cs, int64_t nkv
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)cs, (unsigned)nkv, (unsigned)rows);
-    cfg.blockDim = dim3(kAttnThreads);
+    cfg.blockDim = dim3(kRaThreads);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -169,11 +192,11 @@ template <int GRP, int D>
 static int cluster_size() {
     static int cs = 0;
     if (cs == 0) {
-        auto kern = attn_rope_decode_kernel<GRP, D>;
+        auto kern = attn_rope_decode_kernel<GRP, D, 16>;
         cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(16, 1, 1);
-        cfg.blockDim = dim3(kAttnThreads);
+        cfg.blockDim = dim3(kRaThreads);
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 16;
@@ -194,7 +217,8 @@ static bool dispatch_rope_attn(const RopeAttnParams& p, int grp, int64_t nkv, in
     switch (grp) {
 #define AMCU_RA(G)                                                                   \
     case G: {                                                                        \
-        const cudaError_t e = launch_rope_attn<G, D>(p, cluster_size<G, D>(), nkv, rows, s); \
+        const cudaError_t e = cluster_size<G, D>() == 16 ? launch_rope_attn<G, D, 16>(p, nkv, rows, s)   \
+                                                         : launch_rope_attn<G, D, 8>(p, nkv, rows, s);    \
         (void)e;                                                                     \
         return true;                                                                 \
     }

@@ -235,25 +235,30 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
     pdl_wait();
     pdl_trigger();
 
-    // ---- stage activations [m][k] (+16 B per row) and, for INT4, per-group sums of x
+    // ---- stage the activations [m][k] (+16 B per row): copy, RMSNorm factors
+    // (fused norm), then for INT4 one pass that normalizes, converts to fp16
+    // and sums every 128-column group.
     constexpr int NT = kGemvConsumers * 32;
-    {
-        const int chunks = (int)(p.k / 8);
-        const __nv_bfloat16* xg = static_cast<const __nv_bfloat16*>(p.x);
-        for (int i = threadIdx.x; i < M * chunks; i += NT) {
-            const int m = i / chunks, c = i - m * chunks;
-            *reinterpret_cast<uint4*>(xs + m * xrow + c * 16) = ld_u4(xg + m * p.x_stride + c * 8);
-        }
+    __shared__ float row_mul[kGemvMaxM];  // epilogue multiplier per activation row (a power of two)
+    __shared__ float row_inv[kGemvMaxM];  // RMSNorm factor per row
+    __shared__ unsigned int row_big;      // bit m: row m needs a multiplier above 1 (fp16 overflow guard)
+    const int chunks = (int)(p.k / 8);    // 16-byte chunks per row
+    const __nv_bfloat16* xg = static_cast<const __nv_bfloat16*>(p.x);
+    const __nv_bfloat16* nwt = static_cast<const __nv_bfloat16*>(p.norm_w);
+    if (threadIdx.x < kGemvMaxM) row_mul[threadIdx.x] = 1.f;
+    if (threadIdx.x == 0) row_big = 0u;
+    for (int i = threadIdx.x; i < M * chunks; i += NT) {
+        const int m = i / chunks, c = i - m * chunks;
+        *reinterpret_cast<uint4*>(xs + m * xrow + c * 16) = ld_u4(xg + m * p.x_stride + c * 8);
     }
     named_bar_sync(2, NT);
     if (p.norm_w) {
-        // fused RMSNorm of the staged rows: warp w owns rows w, w + 8, ... as
-        // y = round(x * (mean(x^2) + eps)^-1/2 * w) (the RMSNorm kernel's formula)
-        float* inv_s = reinterpret_cast<float*>(red);  // red is free until the first row-block end
+        // row m's factor (mean(x^2) + eps)^-1/2, reduced by warp m % 8 in a
+        // fixed order; y = round(x * factor * w) as the RMSNorm kernel computes it
         for (int m = warp; m < M; m += kGemvConsumers) {
             const uint8_t* xr = xs + m * xrow;
             float ss = 0.f;
-            for (int c = lane; c < (int)(p.k / 8); c += 32) {
+            for (int c = lane; c < chunks; c += 32) {
                 const uint4 v = *reinterpret_cast<const uint4*>(xr + c * 16);
                 const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -263,91 +268,127 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
                 }
             }
             ss = warp_sum(ss);
-            if (lane == 0) inv_s[m] = 1.0f / sqrtf(ss / (float)p.k + p.eps);
+            if (lane == 0) row_inv[m] = 1.0f / sqrtf(ss / (float)p.k + p.eps);
         }
         named_bar_sync(2, NT);
-        const int chunks = (int)(p.k / 8);
-        const __nv_bfloat16* nwt = static_cast<const __nv_bfloat16*>(p.norm_w);
+    }
+    // normalized bf16 value of element pair j of a 16-byte chunk (a: x bits, w: norm weight bits)
+    auto norm2 = [&](uint32_t a, uint32_t w, float inv, float& lo, float& hi) {
+        lo = __uint_as_float(a << 16);
+        hi = __uint_as_float(a & 0xffff0000u);
+        if (p.norm_w) {
+            lo = Act<__nv_bfloat16>::round(lo * inv * __uint_as_float(w << 16));
+            hi = Act<__nv_bfloat16>::round(hi * inv * __uint_as_float(w & 0xffff0000u));
+        }
+    };
+    if constexpr (W4) {
+        // one thread per 16-column segment (8 per group): normalize, convert
+        // to fp16 (times 1/row_mul), sum; the group sum is a shuffle over the
+        // segment's 8 lanes
+        auto convert_pass = [&](bool redo) {
+            const int segs = G * 8 * M;
+            for (int s0 = 0; s0 < segs; s0 += NT) {
+                const int s = s0 + threadIdx.x;
+                float sum = 0.f;
+                int m = 0, grp = 0;
+                bool active = s < segs;
+                if (active) {
+                    m = s / (G * 8);
+                    const int r = s - m * G * 8;
+                    grp = r >> 3;
+                    active = !redo || ((row_big >> m) & 1u);
+                    if (active) {
+                        const int c0 = grp * 16 + (r & 7) * 2;  // first 16-byte chunk of the segment
+                        uint4* xp = reinterpret_cast<uint4*>(xs + m * xrow + c0 * 16);
+                        uint4 v[2], wv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+                        if (redo) {
+                            v[0] = ld_u4(xg + m * p.x_stride + c0 * 8);
+                            v[1] = ld_u4(xg + m * p.x_stride + c0 * 8 + 8);
+                        } else {
+                            v[0] = xp[0];
+                            v[1] = xp[1];
+                        }
+                        if (p.norm_w) {
+                            wv[0] = ld_u4(nwt + c0 * 8);
+                            wv[1] = ld_u4(nwt + c0 * 8 + 8);
+                        }
+                        const float inv = p.norm_w ? row_inv[m] : 1.f, mul = 1.0f / row_mul[m];
+                        const uint32_t a[8] = {v[0].x, v[0].y, v[0].z, v[0].w, v[1].x, v[1].y, v[1].z, v[1].w};
+                        const uint32_t w[8] = {wv[0].x, wv[0].y, wv[0].z, wv[0].w, wv[1].x, wv[1].y, wv[1].z, wv[1].w};
+                        uint32_t h[8];
+                        float amax = 0.f;
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            float lo, hi;
+                            norm2(a[j], w[j], inv, lo, hi);
+                            amax = fmaxf(amax, fmaxf(fabsf(lo), fabsf(hi)));
+                            const __half2 hv = __floats2half2_rn(lo * mul, hi * mul);
+                            sum += __low2float(hv) + __high2float(hv);
+                            h[j] = *reinterpret_cast<const uint32_t*>(&hv);
+                        }
+                        if (!redo && amax > 32768.f) atomicOr(&row_big, 1u << m);
+                        xp[0] = make_uint4(h[0], h[1], h[2], h[3]);
+                        xp[1] = make_uint4(h[4], h[5], h[6], h[7]);
+                    }
+                }
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+                if (active && (s & 7) == 0) sx[grp * 8 + m] = sum;
+            }
+        };
+        convert_pass(false);
+        for (int i = threadIdx.x; i < G * 8; i += NT)
+            if ((i & 7) >= M) sx[i] = 0.f;  // rows without activations add nothing
+        named_bar_sync(2, NT);
+        if (row_big != 0u) {
+            // Rare: a row reaches 2^15, beyond what fp16 staging keeps. Find
+            // its max, stage it again times 2^-e (exact) and let the epilogue
+            // multiply by 2^e.
+            __shared__ unsigned int row_amax[kGemvMaxM];
+            if (threadIdx.x < kGemvMaxM) row_amax[threadIdx.x] = 0u;
+            named_bar_sync(2, NT);
+            for (int i = threadIdx.x; i < M * chunks; i += NT) {
+                const int m = i / chunks, c = i - m * chunks;
+                if (!((row_big >> m) & 1u)) continue;
+                const uint4 v = ld_u4(xg + m * p.x_stride + c * 8);
+                const uint4 wv = p.norm_w ? ld_u4(nwt + c * 8) : make_uint4(0, 0, 0, 0);
+                const uint32_t a[4] = {v.x, v.y, v.z, v.w}, w[4] = {wv.x, wv.y, wv.z, wv.w};
+                float amax = 0.f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float lo, hi;
+                    norm2(a[j], w[j], p.norm_w ? row_inv[m] : 1.f, lo, hi);
+                    amax = fmaxf(amax, fmaxf(fabsf(lo), fabsf(hi)));
+                }
+                atomicMax(&row_amax[m], __float_as_uint(amax));
+            }
+            named_bar_sync(2, NT);
+            if (threadIdx.x < M && ((row_big >> threadIdx.x) & 1u)) {
+                // e = exponent(max) - 14 keeps the scaled max below 2^15
+                const int e = (int)((row_amax[threadIdx.x] >> 23) & 0xff) - 127 - 14;
+                row_mul[threadIdx.x] = __int_as_float((127 + (e > 0 ? e : 0)) << 23);
+            }
+            named_bar_sync(2, NT);
+            convert_pass(true);
+            named_bar_sync(2, NT);
+        }
+    } else if (p.norm_w) {
         for (int i = threadIdx.x; i < M * chunks; i += NT) {
             const int m = i / chunks, c = i - m * chunks;
             uint4* xp = reinterpret_cast<uint4*>(xs + m * xrow + c * 16);
             const uint4 v = *xp, wv = ld_u4(nwt + c * 8);
-            const float inv = inv_s[m];
-            const uint32_t a[4] = {v.x, v.y, v.z, v.w}, b[4] = {wv.x, wv.y, wv.z, wv.w};
+            const uint32_t a[4] = {v.x, v.y, v.z, v.w}, w[4] = {wv.x, wv.y, wv.z, wv.w};
             uint32_t o[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const float lo = __uint_as_float(a[j] << 16) * inv * __uint_as_float(b[j] << 16);
-                const float hi = __uint_as_float(a[j] & 0xffff0000u) * inv * __uint_as_float(b[j] & 0xffff0000u);
+                float lo, hi;
+                norm2(a[j], w[j], row_inv[m], lo, hi);
                 __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
                 o[j] = *reinterpret_cast<uint32_t*>(&h2);
             }
             *xp = make_uint4(o[0], o[1], o[2], o[3]);
         }
-        named_bar_sync(2, NT);
-    }
-    __shared__ float row_mul[kGemvMaxM];  // epilogue multiplier per activation row
-    if constexpr (W4) {
-        // Overflow guard for the fp16 staging: rows with max |x| > 2^15 are
-        // scaled by 2^-e (exact) and the epilogue multiplies by 2^e.
-        __shared__ unsigned int row_amax[kGemvMaxM];
-        if (threadIdx.x < kGemvMaxM) row_amax[threadIdx.x] = 0u;
-        named_bar_sync(2, NT);
-        {
-            const int chunks = (int)(p.k / 8);
-            for (int i = threadIdx.x; i < M * chunks; i += NT) {
-                const int m = i / chunks, c = i - m * chunks;
-                const uint4 v = *reinterpret_cast<const uint4*>(xs + m * xrow + c * 16);
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-                uint32_t mx = 0;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) mx = max(mx, max((w[j] << 16) & 0x7fffffffu, w[j] & 0x7fff0000u));
-                if (mx > 0x47000000u) atomicMax(&row_amax[m], mx);  // only rows above 2^15 matter
-            }
-        }
-        named_bar_sync(2, NT);
-        if (threadIdx.x < kGemvMaxM) {
-            const unsigned int mx = row_amax[threadIdx.x];
-            // e = exponent(max) - 15 for max >= 2^15 (one more keeps the rounded max below 2^16)
-            const int e = mx > 0x47000000u ? (int)((mx >> 23) & 0xff) - 127 - 15 + 1 : 0;
-            row_mul[threadIdx.x] = __int_as_float((127 + e) << 23);
-        }
-        named_bar_sync(2, NT);
-        // convert to fp16 in place (times 2^-e) and sum each 128-column group
-        const int segs = G * 8 * M;  // 16-column segments, 8 per group
-        for (int s0 = 0; s0 < segs; s0 += NT) {
-            const int s = s0 + threadIdx.x;
-            float sum = 0.f;
-            int m = 0, grp = 0;
-            if (s < segs) {
-                m = s / (G * 8);
-                const int r = s - m * G * 8;
-                grp = r >> 3;
-                uint4* xp = reinterpret_cast<uint4*>(xs + m * xrow + (grp * 128 + (r & 7) * 16) * 2);
-                const float inv = 1.0f / row_mul[m];  // exact: a power of two
-                const uint4 a = xp[0], b = xp[1];
-                const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-                uint32_t h[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const __half2 v = __floats2half2_rn(__uint_as_float(w[j] << 16) * inv,
-                                                        __uint_as_float(w[j] & 0xffff0000u) * inv);
-                    sum += __low2float(v) + __high2float(v);
-                    h[j] = *reinterpret_cast<const uint32_t*>(&v);
-                }
-                xp[0] = make_uint4(h[0], h[1], h[2], h[3]);
-                xp[1] = make_uint4(h[4], h[5], h[6], h[7]);
-            }
-            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-            if (s < segs && (s & 7) == 0) sx[grp * 8 + m] = sum;
-        }
-        for (int i = threadIdx.x; i < G * 8; i += NT)
-            if ((i & 7) >= M) sx[i] = 0.f;  // rows without activations add nothing
-        named_bar_sync(2, NT);
-    } else {
-        if (threadIdx.x < kGemvMaxM) row_mul[threadIdx.x] = 1.f;
         named_bar_sync(2, NT);
     }
     const float rm0 = 2 * t < M ? row_mul[2 * t] : 1.f, rm1 = 2 * t + 1 < M ? row_mul[2 * t + 1] : 1.f;

@@ -174,10 +174,14 @@ def _linear_args(x: torch.Tensor, pw: PackedWeight, epilogue: int, residual, out
 
 
 def linear(x: torch.Tensor, pw: PackedWeight, epilogue: int = L.EPI_STORE, residual: torch.Tensor | None = None,
-           out: torch.Tensor | None = None, entry: str = "amcu_linear") -> torch.Tensor:
-    """y = x @ W^T with the chosen epilogue, through `entry` (amcu_linear by default)."""
-    _require_cuda(x, residual)
+           out: torch.Tensor | None = None, entry: str = "amcu_linear", norm_weight: torch.Tensor | None = None,
+           norm_eps: float = 1e-5) -> torch.Tensor:
+    """y = x @ W^T with the chosen epilogue, through `entry` (amcu_linear by
+    default); with norm_weight, x is RMS-normalized first (fused, decode GEMV)."""
+    _require_cuda(x, residual, norm_weight)
     a, y, ws = _linear_args(x, pw, epilogue, residual, out)
+    if norm_weight is not None:
+        a.norm_weight, a.norm_eps = _p(norm_weight), norm_eps
     check(getattr(lib(), entry)(C.byref(a), _stream()), entry)
     del ws
     return y

@@ -162,6 +162,37 @@ def test_gemv_matches_oracle(ops, orc, fmt, m, n):
 
 
 @pytest.mark.parametrize("fmt", ["int4", "int8"])
+@pytest.mark.parametrize("m", [1, 5])
+def test_gemv_fused_rmsnorm_matches_oracle(ops, orc, fmt, m):
+    """norm_weight: RMSNorm of x fused into the GEMV's staging == RMSNorm
+    (bf16 output) then the GEMV."""
+    n, k = 64, 4096
+    pw, host = _w(ops, orc, fmt, n, k, seed=21)
+    rng = np.random.default_rng(m + 40)
+    x = orc.bf16_round(rng.normal(0, 3, (m, k)).astype(np.float32))
+    w = orc.bf16_round(rng.uniform(0.5, 1.5, k).astype(np.float32))
+    y = ops.linear(bf16_dev(x), pw, norm_weight=bf16_dev(w))
+    h = orc.rmsnorm(x, w, 1e-5, bf=True)
+    np.testing.assert_allclose(to_np(y), _oracle_linear(orc, fmt, h, host), rtol=BF_RTOL, atol=BF_ATOL)
+
+
+@pytest.mark.parametrize("scale", [1e3, 3e5])
+def test_gemv_w4_large_activations(ops, orc, scale):
+    """Rows beyond fp16's range take the staging's power-of-two guard: one row
+    scaled up, one normal row, both against the oracle."""
+    n, k = 64, 1024
+    pw, host = _w(ops, orc, "int4", n, k, seed=22)
+    rng = np.random.default_rng(5)
+    x = rng.normal(0, 1, (2, k)).astype(np.float32)
+    x[0] *= scale
+    x = orc.bf16_round(x)
+    y = to_np(ops.linear(bf16_dev(x), pw))
+    ref = _oracle_linear(orc, "int4", x, host)
+    np.testing.assert_allclose(y, ref, rtol=BF_RTOL, atol=BF_ATOL * scale)
+    assert np.isfinite(y).all()
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
 @pytest.mark.parametrize("m", [1, 3])
 @pytest.mark.parametrize("k", [384, 1792, 14336])
 def test_gemv_stream_geometries(ops, orc, fmt, m, k):

@@ -1,13 +1,465 @@
-// Prefill dequant GEMM on the tcgen05 tensor cores.
+// Prefill dequant GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// y[m, n] = sum_k x[m, k] * w[n, k] for m > 8 rows (prefill), x bf16 and w
+// the quantized device format of gemv.cu (INT4 pair records with inline group
+// scales, or INT8 tiles with per-row scales).
+//
+// A CTA computes a 128 x 128 output tile, K in blocks of 128 (one INT4 scale
+// group), through a ring of kStages shared-memory stages. Warp roles:
+//   warps 0-7  dequantize: warp w turns the 16-row block w of the tile's
+//              weights into bf16 (INT4: q * group scale, rounded once; INT8:
+//              q exactly) written straight into the 128-byte-swizzled K-major
+//              layout the MMA reads; afterwards the same warps are the
+//              epilogue (TMEM -> registers -> bf16 outputs).
+//   warp 8     TMA producer: the x tile, 128 rows x 128 columns, as two
+//              128-byte-swizzled boxes per stage.
+//   warp 9     MMA issuer: one elected thread issues tcgen05.mma
+//              (kind::f16, bf16 x bf16 -> fp32, M = N = 128, K = 16) into a
+//              128-column TMEM accumulator and commits each stage back to
+//              the producers through an mbarrier; warp 9 also owns the TMEM
+//              allocation.
+// Every wait on an mbarrier is bounded: a wait that runs out records an
+// error code in the device error word and the CTA finishes its control flow
+// without waiting again (results are then garbage, and the host sees the
+// code), so a fault of the pipeline cannot hang the GPU.
+#include <cuda.h>
+
 #include "../amcu_internal.h"
+#include "common.cuh"
 #include "gemm_tc.cuh"
+#include "gemv.cuh"
 
 namespace amcu {
 
-bool gemm_tc_supported(const GemmTcParams&, int) { return false; }
+constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 128;
+constexpr int kTcStages = 3;
+constexpr int kTcDequantWarps = 8;
+constexpr int kTcThreads = (kTcDequantWarps + 2) * 32;
+constexpr int kTcTileBytes = kTcBM * kTcBK * 2;  // 32 KB per operand per stage (bf16)
+constexpr int kTcSmemBytes = 1024 + 2 * kTcStages * kTcTileBytes + 256;
+constexpr int32_t kErrGemmTcWait = 0x201;
+
+struct GemmTcKParams {
+    const uint8_t* w;
+    const float* scales;  // INT8 per-row scales
+    __nv_bfloat16* y;
+    const __nv_bfloat16* residual;
+    int64_t m, n, k;
+    int64_t y_stride;
+    int32_t* err;
+};
+
+// ---- tcgen05 / TMA helpers (inline PTX) ----
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major operand in the 128-byte
+// swizzle layout: rows of 128 bytes, 8-row atoms 1024 bytes apart.
+__device__ __forceinline__ uint64_t tc_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address
+    d |= (uint64_t)1 << 16;                    // leading byte offset (unused when swizzled)
+    d |= (uint64_t)(1024 >> 4) << 32;          // stride byte offset: next 8-row atom
+    d |= (uint64_t)1 << 46;                    // descriptor version
+    d |= (uint64_t)2 << 61;                    // 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor: kind::f16, D fp32, A and B bf16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t tc_idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+            " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+            : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                    smem_u32(dst)),
+            "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+            : "memory");
+}
+// 32 lanes x 32 consecutive columns of 32-bit TMEM cells -> 32 registers per thread.
+__device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+              "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+              "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+              "=r"(r[30]), "=r"(r[31])
+            : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of 16-byte chunk c (0..15 over the 128 K columns) of row r in
+// a 128 x 128 bf16 operand tile: two 64-column halves of 16 KB, each rows of
+// 128 bytes with the 16-byte chunks XOR-swizzled by row % 8.
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
+    return (uint32_t)((c >> 3) * 16384 + (r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// Eight bf16 of (q * s) from eight two's-complement nibbles given in order.
+__device__ __forceinline__ uint4 dequant8_w4(const uint32_t (&nib)[8], float s) {
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float a = (__uint_as_float(0x4B000000u | (nib[2 * i] ^ 8u)) - 8388616.0f) * s;
+        const float b = (__uint_as_float(0x4B000000u | (nib[2 * i + 1] ^ 8u)) - 8388616.0f) * s;
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        o[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+// Eight bf16 holding eight int8 exactly.
+__device__ __forceinline__ uint4 dequant8_w8(uint2 v) {
+    const uint32_t w[2] = {v.x, v.y};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint32_t u = w[i] ^ 0x80808080u;
+        float f[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+            f[b] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650u + b)) - 8388736.0f;
+        __nv_bfloat162 p0 = __floats2bfloat162_rn(f[0], f[1]), p1 = __floats2bfloat162_rn(f[2], f[3]);
+        o[2 * i] = *reinterpret_cast<uint32_t*>(&p0);
+        o[2 * i + 1] = *reinterpret_cast<uint32_t*>(&p1);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Warp `wb`'s 16 rows x 128 columns of the weight tile for K block kb, in
+// bf16, into the swizzled stage B. Rows beyond n are zero.
+template <int FMT>
+__device__ __forceinline__ void dequant_rows(const GemmTcKParams& p, int64_t rb, int kb, int wb, int lane,
+                                             uint8_t* B) {
+    const int g = lane >> 2, t = lane & 3;
+    const int r0 = wb * 16 + g, r1 = r0 + 8;  // rows of the tile this lane fills
+    if (rb * 16 >= p.n) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            *reinterpret_cast<uint4*>(B + sw128_offset(r0, 4 * t + c)) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(B + sw128_offset(r1, 4 * t + c)) = make_uint4(0, 0, 0, 0);
+        }
+        return;
+    }
+    if constexpr (FMT == AMCU_WFMT_INT4) {
+        const int64_t G = p.k / 128;
+        const uint8_t* rec = p.w + ((size_t)rb * G + kb) * kW4PairBytes;
+        const uint32_t sv = __ldg(reinterpret_cast<const unsigned int*>(rec + 1024 + 4 * g));
+        const __half2 s2 = *reinterpret_cast<const __half2*>(&sv);
+        const float s_lo = __low2float(s2), s_hi = __high2float(s2);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(rec + h * 512 + lane * 16));
+            const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+            // word j: columns 16t+4j .. +3; nibbles p0,p4,p2,p6 row g and p1,p5,p3,p7 row g+8
+            uint32_t lo[16], hi[16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                // nibble p at bits 4p: row g columns +0..+3 are p0, p4, p2, p6; row g+8 p1, p5, p3, p7
+                lo[4 * j + 0] = (w[j] >> 0) & 15u;
+                lo[4 * j + 1] = (w[j] >> 16) & 15u;
+                lo[4 * j + 2] = (w[j] >> 8) & 15u;
+                lo[4 * j + 3] = (w[j] >> 24) & 15u;
+                hi[4 * j + 0] = (w[j] >> 4) & 15u;
+                hi[4 * j + 1] = (w[j] >> 20) & 15u;
+                hi[4 * j + 2] = (w[j] >> 12) & 15u;
+                hi[4 * j + 3] = (w[j] >> 28) & 15u;
+            }
+            // columns h*64 + 16t + [0, 8) and [8, 16): chunks 8h + 2t and 8h + 2t + 1
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t a[8], b[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    a[e] = lo[8 * c + e];
+                    b[e] = hi[8 * c + e];
+                }
+                *reinterpret_cast<uint4*>(B + sw128_offset(r0, 8 * h + 2 * t + c)) = dequant8_w4(a, s_lo);
+                *reinterpret_cast<uint4*>(B + sw128_offset(r1, 8 * h + 2 * t + c)) = dequant8_w4(b, s_hi);
+            }
+        }
+    } else {
+        const int64_t C = p.k / 64;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint8_t* tile = p.w + ((size_t)rb * C + 2 * kb + h) * 1024;
+            // 32 bytes per lane: row g columns [16t, 16t+16) then row g+8
+            const uint4 va = __ldg(reinterpret_cast<const uint4*>(tile + lane * 32));
+            const uint4 vb = __ldg(reinterpret_cast<const uint4*>(tile + lane * 32 + 16));
+            *reinterpret_cast<uint4*>(B + sw128_offset(r0, 8 * h + 2 * t)) = dequant8_w8(make_uint2(va.x, va.y));
+            *reinterpret_cast<uint4*>(B + sw128_offset(r0, 8 * h + 2 * t + 1)) = dequant8_w8(make_uint2(va.z, va.w));
+            *reinterpret_cast<uint4*>(B + sw128_offset(r1, 8 * h + 2 * t)) = dequant8_w8(make_uint2(vb.x, vb.y));
+            *reinterpret_cast<uint4*>(B + sw128_offset(r1, 8 * h + 2 * t + 1)) = dequant8_w8(make_uint2(vb.z, vb.w));
+        }
+    }
+}
+
+template <int FMT, int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmx,
+                                                                 GemmTcKParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* As = smem;                                  // [kTcStages][32 KB]
+    uint8_t* Bs = smem + kTcStages * kTcTileBytes;       // [kTcStages][32 KB]
+    uint64_t* full_a = reinterpret_cast<uint64_t*>(Bs + kTcStages * kTcTileBytes);
+    uint64_t* full_b = full_a + kTcStages;
+    uint64_t* empty = full_b + kTcStages;
+    uint64_t* accf = empty + kTcStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kTcBM;
+    const int64_t n0 = (int64_t)blockIdx.y * kTcBN;
+    const int KB = (int)(p.k / kTcBK);
+
+    if (warp == kTcDequantWarps + 1) {
+        if (lane == 0) {
+            for (int s = 0; s < kTcStages; ++s) {
+                mbar_init(&full_a[s], 1);
+                mbar_init(&full_b[s], kTcDequantWarps);
+                mbar_init(&empty[s], 1);
+            }
+            mbar_init(accf, 1);
+            fence_mbar_init();
+        }
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTcBN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = *tmem_slot;
+    bool ok = true;
+
+    if (warp == kTcDequantWarps) {
+        // ---- TMA producer: x tiles (the activations come from the previous kernel)
+        pdl_wait();
+        if (lane == 0) {
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % kTcStages;
+                if (kb >= kTcStages && ok && !mbar_wait(&empty[s], ((kb / kTcStages) & 1) ^ 1)) {
+                    ok = false;
+                    record_device_error(p.err, kErrGemmTcWait);
+                }
+                if (!ok) break;
+                mbar_expect_tx(&full_a[s], kTcTileBytes);
+                uint8_t* dst = As + s * kTcTileBytes;
+                tma_load_2d(dst, &tmx, kb * kTcBK, m0, &full_a[s]);
+                tma_load_2d(dst + kTcTileBytes / 2, &tmx, kb * kTcBK + 64, m0, &full_a[s]);
+            }
+        }
+    } else if (warp == kTcDequantWarps + 1) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc_idesc_bf16(kTcBM, kTcBN);
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % kTcStages;
+                const uint32_t par = (kb / kTcStages) & 1;
+                if (ok && (!mbar_wait(&full_a[s], par) || !mbar_wait(&full_b[s], par))) {
+                    ok = false;
+                    record_device_error(p.err, kErrGemmTcWait);
+                }
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(As + s * kTcTileBytes), b0 = smem_u32(Bs + s * kTcTileBytes);
+#pragma unroll
+                for (int j = 0; j < kTcBK / 16; ++j) {
+                    // K step j: half j / 4 of the tile, 32 bytes per step inside the swizzled rows
+                    const uint32_t off = (uint32_t)((j >> 2) * (kTcTileBytes / 2) + (j & 3) * 32);
+                    tc_mma(taddr, tc_desc_sw128(a0 + off), tc_desc_sw128(b0 + off), idesc, (kb | j) != 0);
+                }
+                tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+            }
+            tc_commit(accf);  // all MMAs done: the accumulator is final
+        }
+    } else {
+        // ---- dequant warps (weights do not depend on the previous kernel)
+        const int64_t rb = n0 / 16 + warp;
+        for (int kb = 0; kb < KB; ++kb) {
+            const int s = kb % kTcStages;
+            if (kb >= kTcStages && ok && !mbar_wait(&empty[s], ((kb / kTcStages) & 1) ^ 1)) {
+                ok = false;
+                if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
+            }
+            if (!ok) break;
+            dequant_rows<FMT>(p, rb, kb, warp, lane, Bs + s * kTcTileBytes);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_b[s]);
+        }
+        // ---- epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (tile rows),
+        // columns 64 * (w / 4) .. + 63
+        pdl_wait();
+        if (ok && !mbar_wait(accf, 0)) {
+            ok = false;
+            if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
+        }
+        tc_fence_after();
+        const int quarter = warp & 3, half = warp >> 2;
+        const int row = m0 + quarter * 32 + lane;
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+            uint32_t r[32];
+            const int col0 = half * 64 + cb * 32;
+            tc_ld_32x32b_x32(taddr + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0, r);
+            if (row >= p.m || !ok) continue;
+            if constexpr (EPI == AMCU_EPI_SILU_MUL) {
+                // columns in 16-groups: 8 gate then the matching 8 up rows of the weight
+#pragma unroll
+                for (int gq = 0; gq < 2; ++gq) {
+                    const int64_t nb = n0 + col0 + gq * 16;  // first weight row of the group
+                    if (nb >= p.n) break;
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 8; e += 2) {
+                        float v[2];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            float gt = __uint_as_float(r[gq * 16 + e + u]), up = __uint_as_float(r[gq * 16 + 8 + e + u]);
+                            if constexpr (FMT == AMCU_WFMT_INT8) {
+                                gt *= p.scales[nb + e + u];
+                                up *= p.scales[nb + 8 + e + u];
+                            }
+                            gt = Act<__nv_bfloat16>::round(gt);
+                            up = Act<__nv_bfloat16>::round(up);
+                            v[u] = silu_ref(gt) * up;
+                        }
+                        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[0], v[1]);
+                        o[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
+                    }
+                    *reinterpret_cast<uint4*>(p.y + (int64_t)row * p.y_stride + nb / 2) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            } else {
+#pragma unroll
+                for (int e8 = 0; e8 < 32; e8 += 8) {
+                    const int64_t nc = n0 + col0 + e8;
+                    if (nc >= p.n) break;
+                    uint4 res = make_uint4(0, 0, 0, 0);
+                    if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD)
+                        res = *reinterpret_cast<const uint4*>(p.residual + (int64_t)row * p.y_stride + nc);
+                    const uint32_t rw[4] = {res.x, res.y, res.z, res.w};
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 8; e += 2) {
+                        float v[2];
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            float a = __uint_as_float(r[e8 + e + u]);
+                            if constexpr (FMT == AMCU_WFMT_INT8) a *= p.scales[nc + e + u];
+                            a = Act<__nv_bfloat16>::round(a);
+                            if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD)
+                                a += __uint_as_float(u == 0 ? rw[e / 2] << 16 : rw[e / 2] & 0xffff0000u);
+                            v[u] = a;
+                        }
+                        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[0], v[1]);
+                        o[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
+                    }
+                    *reinterpret_cast<uint4*>(p.y + (int64_t)row * p.y_stride + nc) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+        }
+        pdl_trigger();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kTcDequantWarps + 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(kTcBN) : "memory");
+    }
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on a particular driver library name).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+bool gemm_tc_supported(const GemmTcParams& p, int fmt) {
+    if (fmt != AMCU_WFMT_INT4 && fmt != AMCU_WFMT_INT8) return false;
+    if (p.k % kTcBK != 0 || p.n % 16 != 0) return false;
+    if ((p.x_stride * 2) % 16 != 0 || (reinterpret_cast<uintptr_t>(p.x) & 15) != 0) return false;
+    if ((reinterpret_cast<uintptr_t>(p.y) & 15) != 0 || (p.y_stride * 2) % 16 != 0) return false;
+    if (p.residual && (reinterpret_cast<uintptr_t>(p.residual) & 15) != 0) return false;
+    if (p.m > 0x7fffffff || p.k > 0x7fffffff) return false;
+    return encode_tiled() != nullptr;
+}
 size_t gemm_tc_workspace_bytes(const GemmTcParams&, int) { return 0; }
-am_status_code launch_gemm_tc(const GemmTcParams&, int, int, cudaStream_t) {
-    return set_error(AM_STATUS_UNIMPLEMENTED, "tcgen05 GEMM not built");
+
+template <int FMT, int EPI>
+static am_status_code launch_tc(const GemmTcParams& g, const CUtensorMap& map, cudaStream_t s) {
+    auto kern = gemm_tc_kernel<FMT, EPI>;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
+        attr = true;
+    }
+    GemmTcKParams p{};
+    p.w = static_cast<const uint8_t*>(g.w);
+    p.scales = static_cast<const float*>(g.scales);
+    p.y = static_cast<__nv_bfloat16*>(g.y);
+    p.residual = static_cast<const __nv_bfloat16*>(g.residual);
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.y_stride = g.y_stride;
+    p.err = device_error_word();
+    const dim3 grid((unsigned)((g.m + kTcBM - 1) / kTcBM), (unsigned)((g.n + kTcBN - 1) / kTcBN));
+    launch_pdl(kern, grid, dim3(kTcThreads), (size_t)kTcSmemBytes, s, map, p);
+    return AM_STATUS_OK;
+}
+
+am_status_code launch_gemm_tc(const GemmTcParams& g, int fmt, int epi, cudaStream_t s) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return set_error(AM_STATUS_UNAVAILABLE, "cuTensorMapEncodeTiled unavailable");
+    // x as a 2-D bf16 tensor [m rows][k columns], boxes of 64 columns x 128 rows, 128-byte swizzle
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)g.k, (cuuint64_t)g.m};
+    const cuuint64_t strides[1] = {(cuuint64_t)g.x_stride * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)kTcBM};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(g.x), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(AM_STATUS_INTERNAL, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+#define AMCU_TC(F, E) return launch_tc<F, E>(g, map, s)
+    if (fmt == AMCU_WFMT_INT4) {
+        if (epi == AMCU_EPI_STORE) AMCU_TC(AMCU_WFMT_INT4, AMCU_EPI_STORE);
+        if (epi == AMCU_EPI_RESIDUAL_ADD) AMCU_TC(AMCU_WFMT_INT4, AMCU_EPI_RESIDUAL_ADD);
+        AMCU_TC(AMCU_WFMT_INT4, AMCU_EPI_SILU_MUL);
+    }
+    if (epi == AMCU_EPI_STORE) AMCU_TC(AMCU_WFMT_INT8, AMCU_EPI_STORE);
+    if (epi == AMCU_EPI_RESIDUAL_ADD) AMCU_TC(AMCU_WFMT_INT8, AMCU_EPI_RESIDUAL_ADD);
+    AMCU_TC(AMCU_WFMT_INT8, AMCU_EPI_SILU_MUL);
+#undef AMCU_TC
 }
 
 }  // namespace amcu

@@ -224,6 +224,35 @@ def test_prefill_gemm_matches_torch_fp32(ops, orc, fmt, m):
 
 
 @pytest.mark.parametrize("fmt", ["int4", "int8"])
+def test_prefill_gemm_epilogues_ragged_tiles(ops, orc, fmt):
+    """Tensor-core GEMM with m and n that do not fill the 128 x 128 tiles:
+    residual add (in place) and the gate/up SiLU-Mul epilogue against the
+    oracle on every row."""
+    from aethermind_b200 import _lib as L
+    m, k, n, inter = 200, 1024, 2064, 520
+    rng = np.random.default_rng(12)
+    x = orc.bf16_round(rng.normal(0, 1, (m, k)).astype(np.float32))
+    res = orc.bf16_round(rng.normal(0, 1, (m, n)).astype(np.float32))
+    pw, host = _w(ops, orc, fmt, n, k, seed=13)
+    xr = bf16_dev(res)
+    y = ops.linear(bf16_dev(x), pw, epilogue=L.EPI_RESIDUAL_ADD, residual=xr, out=xr)
+    ref = orc.bf16_round(res + _oracle_linear(orc, fmt, x, host))
+    np.testing.assert_allclose(to_np(y), ref, rtol=BF_RTOL, atol=5e-2)
+    syn = ops.synth_w4 if fmt == "int4" else ops.synth_w8
+    base = orc.W4_BASE if fmt == "int4" else orc.W8_BASE
+    f = L.WFMT_INT4 if fmt == "int4" else L.WFMT_INT8
+    gq, gs = syn(14, 1, inter, k, base)
+    uq, us = syn(14, 2, inter, k, base)
+    gu = ops.prepack_gate_up(f, gq, gs, uq, us, inter, k)
+    hs = (lambda s: s.cpu().numpy().view(np.uint16)) if fmt == "int4" else (lambda s: s.cpu().numpy())
+    g = _oracle_linear(orc, fmt, x, (gq.cpu().numpy(), hs(gs)))
+    u = _oracle_linear(orc, fmt, x, (uq.cpu().numpy(), hs(us)))
+    a = ops.linear(bf16_dev(x), gu, epilogue=L.EPI_SILU_MUL)
+    ref = orc.silu_mul(orc.bf16_round(g), orc.bf16_round(u), bf=True)
+    np.testing.assert_allclose(to_np(a), ref, rtol=BF_RTOL, atol=5e-2)
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
 def test_linear_residual_and_silu_epilogues(ops, orc, fmt):
     from aethermind_b200 import _lib as L
     m, k, inter, n = 4, 4096, 1024, 2048
@@ -250,12 +279,15 @@ def test_linear_residual_and_silu_epilogues(ops, orc, fmt):
         u = orc.linear_w8(x, uq.cpu().numpy(), us.cpu().numpy())
     y = ops.linear(bf16_dev(x), gu, epilogue=L.EPI_SILU_MUL)
     np.testing.assert_allclose(to_np(y), orc.silu_mul(g, u, bf=True), rtol=BF_RTOL, atol=BF_ATOL)
-    # the same weights through the prefill GEMM path (m = 64)
+    # the same weights through the prefill GEMM path (m = 64); the tensor-core
+    # GEMM rounds each dequantized weight q * s to bf16 once, so the SiLU-Mul of
+    # its slightly different gate/up sums can flip a bf16 rounding: atol 5e-2
+    # as for the other GEMM checks
     x64 = orc.bf16_round(rng.normal(0, 1, (64, k)).astype(np.float32))
     y64 = ops.linear(bf16_dev(x64), gu, epilogue=L.EPI_SILU_MUL)
     g64 = _oracle_linear(orc, fmt, x64, (gq.cpu().numpy(), gs.cpu().numpy().view(np.uint16) if fmt == "int4" else gs.cpu().numpy()))
     u64 = _oracle_linear(orc, fmt, x64, (uq.cpu().numpy(), us.cpu().numpy().view(np.uint16) if fmt == "int4" else us.cpu().numpy()))
-    np.testing.assert_allclose(to_np(y64), orc.silu_mul(g64, u64, bf=True), rtol=BF_RTOL, atol=BF_ATOL)
+    np.testing.assert_allclose(to_np(y64), orc.silu_mul(g64, u64, bf=True), rtol=BF_RTOL, atol=5e-2)
 
 
 def test_plain_f32_linear(ops, orc):

@@ -36,7 +36,8 @@ constexpr int kTcStages = 3;
 constexpr int kTcDequantWarps = 8;
 constexpr int kTcThreads = (kTcDequantWarps + 2) * 32;
 constexpr int kTcTileBytes = kTcBM * kTcBK * 2;  // 32 KB per operand per stage (bf16)
-constexpr int kTcSmemBytes = 1024 + 2 * kTcStages * kTcTileBytes + 256;
+constexpr int kTcWStage = kTcDequantWarps * kW4PairBytes;  // INT4 pair records of one stage (8 row blocks)
+constexpr int kTcSmemBytes = 1024 + 2 * kTcStages * kTcTileBytes + (kTcStages + 2) * kTcBN * 4 + kTcStages * kTcWStage + 256;
 constexpr int32_t kErrGemmTcWait = 0x201;
 
 struct GemmTcKParams {
@@ -207,18 +208,141 @@ __device__ __forceinline__ void dequant_rows(const GemmTcKParams& p, int64_t rb,
     }
 }
 
+// INT4, exact: warp wb's 16 rows x 128 columns (pair record `rec`, staged in
+// shared memory by the TMA warp) as the exact bf16 integers q
+// (one LOP3 + one bf16x2 subtract per two weights; word layout as in gemv.cu:
+// (w >> 4i) & 0x000F000F is register i, i = 0/2 row g and 1/3 row g+8), and
+// the rows' group scales as fp32 into scl[row]. Rows beyond n are zero.
+__device__ __forceinline__ void dequant_rows_w4_exact(const GemmTcKParams& p, int64_t rb, const uint8_t* rec, int wb,
+                                                      int lane, uint8_t* B, float* scl) {
+    const int g = lane >> 2, t = lane & 3;
+    const int r0 = wb * 16 + g, r1 = r0 + 8;
+    if (rb * 16 >= p.n) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            *reinterpret_cast<uint4*>(B + sw128_offset(r0, 4 * t + c)) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(B + sw128_offset(r1, 4 * t + c)) = make_uint4(0, 0, 0, 0);
+        }
+        if (t == 0) {
+            scl[r0] = 0.f;
+            scl[r1] = 0.f;
+        }
+        return;
+    }
+    if (t == 0) {
+        const uint32_t sv = *reinterpret_cast<const uint32_t*>(rec + 1024 + 4 * g);
+        const __half2 s2 = *reinterpret_cast<const __half2*>(&sv);
+        scl[r0] = __low2float(s2);
+        scl[r1] = __high2float(s2);
+    }
+    const __nv_bfloat162 bias = __floats2bfloat162_rn(136.f, 136.f);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(rec + h * 512 + lane * 16);
+        const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t reg[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                uint32_t v;
+                asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(v) : "r"(w[j] >> (4 * i)), "r"(0x000F000Fu), "r"(0x43084308u));
+                __nv_bfloat162 b = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&v), bias);
+                reg[j][i] = *reinterpret_cast<uint32_t*>(&b);
+            }
+        // row g: columns 16t + [0, 8) from words 0-1 (registers 0, 2), [8, 16) from words 2-3
+        *reinterpret_cast<uint4*>(B + sw128_offset(r0, 8 * h + 2 * t)) = make_uint4(reg[0][0], reg[0][2], reg[1][0], reg[1][2]);
+        *reinterpret_cast<uint4*>(B + sw128_offset(r0, 8 * h + 2 * t + 1)) = make_uint4(reg[2][0], reg[2][2], reg[3][0], reg[3][2]);
+        *reinterpret_cast<uint4*>(B + sw128_offset(r1, 8 * h + 2 * t)) = make_uint4(reg[0][1], reg[0][3], reg[1][1], reg[1][3]);
+        *reinterpret_cast<uint4*>(B + sw128_offset(r1, 8 * h + 2 * t + 1)) = make_uint4(reg[2][1], reg[2][3], reg[3][1], reg[3][3]);
+    }
+}
+
+// Stores / epilogue of one thread's 32 accumulated columns col0 .. col0 + 31
+// of output row `row` (values already scaled to the weight's units).
+template <int FMT, int EPI>
+__device__ __forceinline__ void tc_store32(const GemmTcKParams& p, int row, int64_t n0, int col0, const float (&v)[32]) {
+    if constexpr (EPI == AMCU_EPI_SILU_MUL) {
+        // columns in 16-groups: 8 gate then the matching 8 up rows of the weight
+#pragma unroll
+        for (int gq = 0; gq < 2; ++gq) {
+            const int64_t nb = n0 + col0 + gq * 16;  // first weight row of the group
+            if (nb >= p.n) break;
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                float r2[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    float gt = v[gq * 16 + e + u], up = v[gq * 16 + 8 + e + u];
+                    if constexpr (FMT == AMCU_WFMT_INT8) {
+                        gt *= p.scales[nb + e + u];
+                        up *= p.scales[nb + 8 + e + u];
+                    }
+                    gt = Act<__nv_bfloat16>::round(gt);
+                    up = Act<__nv_bfloat16>::round(up);
+                    r2[u] = silu_ref(gt) * up;
+                }
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(r2[0], r2[1]);
+                o[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(p.y + (int64_t)row * p.y_stride + nb / 2) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    } else {
+#pragma unroll
+        for (int e8 = 0; e8 < 32; e8 += 8) {
+            const int64_t nc = n0 + col0 + e8;
+            if (nc >= p.n) break;
+            uint4 res = make_uint4(0, 0, 0, 0);
+            if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD)
+                res = *reinterpret_cast<const uint4*>(p.residual + (int64_t)row * p.y_stride + nc);
+            const uint32_t rw[4] = {res.x, res.y, res.z, res.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+                float r2[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    float a = v[e8 + e + u];
+                    if constexpr (FMT == AMCU_WFMT_INT8) a *= p.scales[nc + e + u];
+                    a = Act<__nv_bfloat16>::round(a);
+                    if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD)
+                        a += __uint_as_float(u == 0 ? rw[e / 2] << 16 : rw[e / 2] & 0xffff0000u);
+                    r2[u] = a;
+                }
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(r2[0], r2[1]);
+                o[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(p.y + (int64_t)row * p.y_stride + nc) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
+// INT4 keeps every 128-column group's product exact: the MMAs of one K block
+// accumulate sum q * x in a fresh TMEM buffer (two buffers, 256 columns), and
+// the dequant warps fold it into registers with the group scale (acc += s *
+// partial) while the tensor cores work on the next block -- the reference's
+// order of operations (sum over groups of scale * integer dot product) up to
+// fp32 rounding. INT8 (one per-row scale) accumulates all of K in TMEM and
+// scales in the epilogue.
 template <int FMT, int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmx,
                                                                  GemmTcKParams p) {
+    constexpr bool W4 = FMT == AMCU_WFMT_INT4;
+    constexpr int kTmemCols = W4 ? 2 * kTcBN : kTcBN;
+    constexpr int kScl = kTcStages + 2;  // scale ring: entry kb % kScl is rewritten only after promotion(kb)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t* As = smem;                                  // [kTcStages][32 KB]
-    uint8_t* Bs = smem + kTcStages * kTcTileBytes;       // [kTcStages][32 KB]
-    uint64_t* full_a = reinterpret_cast<uint64_t*>(Bs + kTcStages * kTcTileBytes);
+    uint8_t* As = smem;                             // [kTcStages][32 KB]
+    uint8_t* Bs = smem + kTcStages * kTcTileBytes;  // [kTcStages][32 KB]
+    float* scl = reinterpret_cast<float*>(Bs + kTcStages * kTcTileBytes);  // [kScl][128]
+    uint8_t* Ws = reinterpret_cast<uint8_t*>(scl + kScl * kTcBN);        // [kTcStages][8 records] (INT4)
+    uint64_t* full_a = reinterpret_cast<uint64_t*>(Ws + (W4 ? kTcStages * kTcWStage : 0));
     uint64_t* full_b = full_a + kTcStages;
     uint64_t* empty = full_b + kTcStages;
-    uint64_t* accf = empty + kTcStages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+    uint64_t* tfull = empty + kTcStages;  // [2] accumulator buffer ready
+    uint64_t* tempty = tfull + 2;         // [2] accumulator buffer read out
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * kTcBM;
@@ -232,12 +356,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 mbar_init(&full_b[s], kTcDequantWarps);
                 mbar_init(&empty[s], 1);
             }
-            mbar_init(accf, 1);
+            for (int b = 0; b < 2; ++b) {
+                mbar_init(&tfull[b], 1);
+                mbar_init(&tempty[b], kTcDequantWarps);
+            }
             fence_mbar_init();
         }
         __syncwarp();
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(kTcBN)
+                     "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -258,10 +385,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                     record_device_error(p.err, kErrGemmTcWait);
                 }
                 if (!ok) break;
-                mbar_expect_tx(&full_a[s], kTcTileBytes);
+                uint32_t bytes = kTcTileBytes;
+                int nrec = 0;
+                if constexpr (W4) {
+                    // the 8 row blocks' pair records of this K block (rows beyond n: none)
+                    const int64_t rem = (p.n - n0) / 16;
+                    nrec = rem < kTcDequantWarps ? (int)rem : kTcDequantWarps;
+                    bytes += (uint32_t)(nrec * kW4PairBytes);
+                }
+                mbar_expect_tx(&full_a[s], bytes);
                 uint8_t* dst = As + s * kTcTileBytes;
                 tma_load_2d(dst, &tmx, kb * kTcBK, m0, &full_a[s]);
                 tma_load_2d(dst + kTcTileBytes / 2, &tmx, kb * kTcBK + 64, m0, &full_a[s]);
+                if constexpr (W4) {
+                    const int64_t G = p.k / 128;
+                    for (int w = 0; w < nrec; ++w)
+                        bulk_g2s(Ws + s * kTcWStage + w * kW4PairBytes,
+                                 p.w + ((size_t)(n0 / 16 + w) * G + kb) * kW4PairBytes, kW4PairBytes, &full_a[s]);
+                }
             }
         }
     } else if (warp == kTcDequantWarps + 1) {
@@ -271,107 +412,108 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             for (int kb = 0; kb < KB; ++kb) {
                 const int s = kb % kTcStages;
                 const uint32_t par = (kb / kTcStages) & 1;
-                if (ok && (!mbar_wait(&full_a[s], par) || !mbar_wait(&full_b[s], par))) {
-                    ok = false;
+                if (ok && (!mbar_wait(&full_a[s], par) || !mbar_wait(&full_b[s], par))) ok = false;
+                if (W4 && ok && kb >= 2 && !mbar_wait(&tempty[kb & 1], ((kb >> 1) & 1) ^ 1)) ok = false;
+                if (!ok) {
                     record_device_error(p.err, kErrGemmTcWait);
+                    break;
                 }
-                if (!ok) break;
                 tc_fence_after();
                 const uint32_t a0 = smem_u32(As + s * kTcTileBytes), b0 = smem_u32(Bs + s * kTcTileBytes);
+                const uint32_t d = W4 ? taddr + (uint32_t)((kb & 1) * kTcBN) : taddr;
 #pragma unroll
                 for (int j = 0; j < kTcBK / 16; ++j) {
                     // K step j: half j / 4 of the tile, 32 bytes per step inside the swizzled rows
                     const uint32_t off = (uint32_t)((j >> 2) * (kTcTileBytes / 2) + (j & 3) * 32);
-                    tc_mma(taddr, tc_desc_sw128(a0 + off), tc_desc_sw128(b0 + off), idesc, (kb | j) != 0);
+                    tc_mma(d, tc_desc_sw128(a0 + off), tc_desc_sw128(b0 + off), idesc, W4 ? (j != 0) : ((kb | j) != 0));
                 }
                 tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+                if (W4) tc_commit(&tfull[kb & 1]);
             }
-            tc_commit(accf);  // all MMAs done: the accumulator is final
+            if (!W4) tc_commit(&tfull[0]);  // all MMAs done: the accumulator is final
         }
     } else {
-        // ---- dequant warps (weights do not depend on the previous kernel)
+        // ---- dequant warps (weights do not depend on the previous kernel) and epilogue
         const int64_t rb = n0 / 16 + warp;
-        for (int kb = 0; kb < KB; ++kb) {
+        const int quarter = warp & 3, half = warp >> 2;
+        const int row = m0 + quarter * 32 + lane;  // TMEM lane of this thread = tile row
+        auto produce = [&](int kb) {
             const int s = kb % kTcStages;
-            if (kb >= kTcStages && ok && !mbar_wait(&empty[s], ((kb / kTcStages) & 1) ^ 1)) {
+            if constexpr (W4) {
+                // the TMA warp staged this stage's records after the stage was released
+                if (ok && !mbar_wait(&full_a[s], (kb / kTcStages) & 1)) {
+                    ok = false;
+                    if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
+                }
+            } else if (kb >= kTcStages && ok && !mbar_wait(&empty[s], ((kb / kTcStages) & 1) ^ 1)) {
                 ok = false;
                 if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
             }
-            if (!ok) break;
-            dequant_rows<FMT>(p, rb, kb, warp, lane, Bs + s * kTcTileBytes);
+            if (!ok) return;
+            if constexpr (W4)
+                dequant_rows_w4_exact(p, rb, Ws + s * kTcWStage + warp * kW4PairBytes, warp, lane, Bs + s * kTcTileBytes,
+                                      scl + (kb % kScl) * kTcBN);
+            else dequant_rows<FMT>(p, rb, kb, warp, lane, Bs + s * kTcTileBytes);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
             __syncwarp();
             if (lane == 0) mbar_arrive(&full_b[s]);
+        };
+        float acc[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+        if constexpr (W4) {
+            for (int kb = 0; kb < kTcStages && kb < KB; ++kb) produce(kb);
+            for (int kb = 0; kb < KB; ++kb) {
+                if (ok && !mbar_wait(&tfull[kb & 1], (kb >> 1) & 1)) {
+                    ok = false;
+                    if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
+                }
+                tc_fence_after();
+                const float* sc = scl + (kb % kScl) * kTcBN + half * 64;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t r[32];
+                    tc_ld_32x32b_x32(taddr + (uint32_t)((kb & 1) * kTcBN) + ((uint32_t)(quarter * 32) << 16) +
+                                             (uint32_t)(half * 64 + c * 32),
+                                     r);
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        const float4 s4 = *reinterpret_cast<const float4*>(sc + c * 32 + i);
+                        acc[c * 32 + i + 0] = fmaf(s4.x, __uint_as_float(r[i + 0]), acc[c * 32 + i + 0]);
+                        acc[c * 32 + i + 1] = fmaf(s4.y, __uint_as_float(r[i + 1]), acc[c * 32 + i + 1]);
+                        acc[c * 32 + i + 2] = fmaf(s4.z, __uint_as_float(r[i + 2]), acc[c * 32 + i + 2]);
+                        acc[c * 32 + i + 3] = fmaf(s4.w, __uint_as_float(r[i + 3]), acc[c * 32 + i + 3]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[kb & 1]);
+                if (kb + kTcStages < KB) produce(kb + kTcStages);
+            }
+        } else {
+            for (int kb = 0; kb < KB; ++kb) produce(kb);
+            if (ok && !mbar_wait(&tfull[0], 0)) {
+                ok = false;
+                if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                uint32_t r[32];
+                tc_ld_32x32b_x32(taddr + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(half * 64 + c * 32), r);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[c * 32 + i] = __uint_as_float(r[i]);
+            }
         }
-        // ---- epilogue: warp w reads TMEM lanes 32 * (w % 4) .. + 31 (tile rows),
-        // columns 64 * (w / 4) .. + 63
+        // ---- epilogue: this thread's row, columns half * 64 .. + 63
         pdl_wait();
-        if (ok && !mbar_wait(accf, 0)) {
-            ok = false;
-            if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
-        }
-        tc_fence_after();
-        const int quarter = warp & 3, half = warp >> 2;
-        const int row = m0 + quarter * 32 + lane;
+        if (row < p.m && ok) {
 #pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {
-            uint32_t r[32];
-            const int col0 = half * 64 + cb * 32;
-            tc_ld_32x32b_x32(taddr + ((uint32_t)(quarter * 32) << 16) + (uint32_t)col0, r);
-            if (row >= p.m || !ok) continue;
-            if constexpr (EPI == AMCU_EPI_SILU_MUL) {
-                // columns in 16-groups: 8 gate then the matching 8 up rows of the weight
+            for (int c = 0; c < 2; ++c) {
+                float v[32];
 #pragma unroll
-                for (int gq = 0; gq < 2; ++gq) {
-                    const int64_t nb = n0 + col0 + gq * 16;  // first weight row of the group
-                    if (nb >= p.n) break;
-                    uint32_t o[4];
-#pragma unroll
-                    for (int e = 0; e < 8; e += 2) {
-                        float v[2];
-#pragma unroll
-                        for (int u = 0; u < 2; ++u) {
-                            float gt = __uint_as_float(r[gq * 16 + e + u]), up = __uint_as_float(r[gq * 16 + 8 + e + u]);
-                            if constexpr (FMT == AMCU_WFMT_INT8) {
-                                gt *= p.scales[nb + e + u];
-                                up *= p.scales[nb + 8 + e + u];
-                            }
-                            gt = Act<__nv_bfloat16>::round(gt);
-                            up = Act<__nv_bfloat16>::round(up);
-                            v[u] = silu_ref(gt) * up;
-                        }
-                        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[0], v[1]);
-                        o[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
-                    }
-                    *reinterpret_cast<uint4*>(p.y + (int64_t)row * p.y_stride + nb / 2) = make_uint4(o[0], o[1], o[2], o[3]);
-                }
-            } else {
-#pragma unroll
-                for (int e8 = 0; e8 < 32; e8 += 8) {
-                    const int64_t nc = n0 + col0 + e8;
-                    if (nc >= p.n) break;
-                    uint4 res = make_uint4(0, 0, 0, 0);
-                    if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD)
-                        res = *reinterpret_cast<const uint4*>(p.residual + (int64_t)row * p.y_stride + nc);
-                    const uint32_t rw[4] = {res.x, res.y, res.z, res.w};
-                    uint32_t o[4];
-#pragma unroll
-                    for (int e = 0; e < 8; e += 2) {
-                        float v[2];
-#pragma unroll
-                        for (int u = 0; u < 2; ++u) {
-                            float a = __uint_as_float(r[e8 + e + u]);
-                            if constexpr (FMT == AMCU_WFMT_INT8) a *= p.scales[nc + e + u];
-                            a = Act<__nv_bfloat16>::round(a);
-                            if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD)
-                                a += __uint_as_float(u == 0 ? rw[e / 2] << 16 : rw[e / 2] & 0xffff0000u);
-                            v[u] = a;
-                        }
-                        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[0], v[1]);
-                        o[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
-                    }
-                    *reinterpret_cast<uint4*>(p.y + (int64_t)row * p.y_stride + nc) = make_uint4(o[0], o[1], o[2], o[3]);
-                }
+                for (int i = 0; i < 32; ++i) v[i] = acc[c * 32 + i];
+                tc_store32<FMT, EPI>(p, row, n0, half * 64 + c * 32, v);
             }
         }
         pdl_trigger();
@@ -380,7 +522,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     __syncthreads();
     if (warp == kTcDequantWarps + 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(kTcBN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(kTmemCols) : "memory");
     }
 }
 

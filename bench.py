@@ -282,14 +282,18 @@ def main() -> None:
                 "h2d_bytes_per_step": PROMPT * 8, "d2h_bytes_per_step": NEW * 12 + 4},
         "gpu_launches": None,
     }
-    # kernel launches of this library in the timed region (from the plans)
+    # kernel launches of this library in the timed region (from the plans): one
+    # per kernel step, plus the split-K combine of an unfused decode attention,
+    # the second pass of the two-phase argmax, and the decode-state advance
     try:
         dec_steps = sess.plan_steps(1, 1, 1)
         pre_steps = sess.plan_steps(0, 1, PROMPT)
-        n_dec = sum(1 for l in dec_steps if "<host>" not in l) + sum(1 for l in dec_steps if "AttnDecode" in l) + 1
-        lin = sum(1 for l in pre_steps if "Gemm" in l)
-        n_pre = sum(1 for l in pre_steps if "<host>" not in l) + lin * (PROMPT // 8 - 1) + 1
-        line["gpu_launches"] = args.steps * (n_pre + (NEW - 1) * n_dec)
+        def launches(steps):
+            n = sum(1 for l in steps if "<host>" not in l)
+            n += sum(1 for l in steps if "AttnDecodeSplitK" in l)
+            n += sum(1 for l in steps if l.split()[0] == "argmax")
+            return n + 1
+        line["gpu_launches"] = args.steps * (launches(pre_steps) + (NEW - 1) * launches(dec_steps))
     except Exception as e:  # pragma: no cover
         line["gpu_launches_error"] = str(e)
     if rank == 0 and world == 1 and not args.no_roofline:

@@ -6,6 +6,11 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+
+#include <dlfcn.h>
+#include <execinfo.h>
+#include <signal.h>
+#include <unistd.h>
 #include <string>
 
 #include "amcu_internal.h"
@@ -108,3 +113,32 @@ const char* am_error_message(am_error_handle e) {
 }
 
 }  // extern "C"
+
+// Diagnostics: with AM_SEGV_TRACE=1 in the environment, a crash of the host
+// process prints the faulting call stack (module and offset of every frame)
+// to stderr before the default action runs.
+namespace {
+void segv_trace(int sig) {
+    void* frames[64];
+    const int n = backtrace(frames, 64);
+    char line[512];
+    for (int i = 0; i < n; ++i) {
+        Dl_info info{};
+        if (dladdr(frames[i], &info) && info.dli_fname) {
+            const int len = snprintf(line, sizeof line, "am-segv #%d %s+0x%lx %s\n", i, info.dli_fname,
+                                     (unsigned long)((char*)frames[i] - (char*)info.dli_fbase),
+                                     info.dli_sname ? info.dli_sname : "");
+            if (len > 0) (void)!write(2, line, (size_t)len < sizeof line ? (size_t)len : sizeof line - 1);
+        }
+    }
+    signal(sig, SIG_DFL);
+    raise(sig);
+}
+struct SegvTraceInstaller {
+    SegvTraceInstaller() {
+        const char* v = std::getenv("AM_SEGV_TRACE");
+        if (v && v[0] == '1') signal(SIGSEGV, segv_trace);
+    }
+} g_segv_trace_installer;
+}  // namespace
+

@@ -560,7 +560,12 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
     while (stages > 2 && gemv_smem<FMT>(1, p.k, sby, stages).total > per_cta) --stages;
     p.stages = stages;
     p.stage_units = su;
-    const int per_sm = smem_per_sm / (gemv_smem<FMT>(1, p.k, sby, stages).total + 1024);
+    int per_sm = smem_per_sm / (gemv_smem<FMT>(1, p.k, sby, stages).total + 1024);
+#ifdef GEMV_GRID_CPS
+    // size the grid for fewer CTAs per SM than fit, leaving room for the next
+    // kernel's CTAs to start (and stream their weights) early
+    if (per_sm > GEMV_GRID_CPS) per_sm = GEMV_GRID_CPS;
+#endif
     const int64_t max_ctas = (int64_t)(per_sm > 0 ? per_sm : 1) * num_sms();
     const int64_t nrb = p.n / 16;
     p.rb_per_cta = (int)((nrb + max_ctas - 1) / max_ctas);

@@ -159,6 +159,9 @@ struct ExecutionPlan {
     ExecPhase phase = ExecPhase::kBoth;
     std::vector<ExecutionStep> steps;
     size_t workspace_bytes = 0;
+    // Contexts of this plan's host steps (ExecutionStep::host_ctx points into
+    // them): they live exactly as long as the plan.
+    std::vector<std::shared_ptr<void>> host_ctx_owned;
 };
 
 class LayerRunner {

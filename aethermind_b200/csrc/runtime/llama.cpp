@@ -310,7 +310,6 @@ struct am_session_s {
     // plans
     aethermind::ExecutionPlan prefill, decode;
     int64_t prefill_B = -1, prefill_R = -1, decode_B = -1;
-    std::vector<std::unique_ptr<aethermind::AllReduceCtx>> ar_ctx;
     cudaGraphExec_t graph = nullptr;
     int64_t graph_B = -1;
     void* pinned = nullptr;
@@ -467,8 +466,6 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
     // the unfused steps
     const bool fuse_attn = phase == ExecPhase::kDecode && R == B && s->cfg.unfused_attention == 0 &&
                            m->rt->backend->ResolveKernelInfo(OpType::kRoPEAttention, act).ok();
-    s->ar_ctx.clear();
-
     // Embedding
     {
         const bool tied_i8 = c.tied_embeddings && wf == WeightFormat::kQuantizedInt8;
@@ -533,13 +530,13 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
             }
             AM_RETURN_IF_ERROR(pb.Add(OpType::kLinear, lin, {in}, {MView2(s->part.data(), A, M, H, H)}, &store, &W.w,
                                       p + name + "_partial"));
-            auto ctx = std::make_unique<AllReduceCtx>(AllReduceCtx{&m->rt->comm, s->part.data(), (size_t)(M * H)});
+            auto ctx = std::make_shared<AllReduceCtx>(AllReduceCtx{&m->rt->comm, s->part.data(), (size_t)(M * H)});
             ExecutionStep st;
             st.label = p + name + "_allreduce";
             st.host_fn = AllReduceStep;
             st.host_ctx = ctx.get();
             plan.steps.push_back(std::move(st));
-            s->ar_ctx.push_back(std::move(ctx));
+            plan.host_ctx_owned.push_back(std::move(ctx));
             return pb.Add(OpType::kAdd, act, {View2(s->x.data(), A, M, H, H), View2(s->part.data(), A, M, H, H)},
                           {MView2(s->x.data(), A, M, H, H)}, (const int*)nullptr, nullptr, p + name + "_residual");
         };

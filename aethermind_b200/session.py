@@ -81,7 +81,10 @@ class Runtime:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown: module globals already cleared
+            pass
 
 
 class Model:
@@ -115,7 +118,10 @@ class Model:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown: module globals already cleared
+            pass
 
 
 class Session:
@@ -169,4 +175,7 @@ class Session:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except TypeError:  # interpreter shutdown: module globals already cleared
+            pass

@@ -96,7 +96,8 @@ class AmModelConfig(C.Structure):
 
 
 class AmSessionConfig(C.Structure):
-    _fields_ = [("max_new_tokens", C.c_int64), ("use_cuda_graph", C.c_int32), ("unfused_attention", C.c_int32)]
+    _fields_ = [("max_new_tokens", C.c_int64), ("use_cuda_graph", C.c_int32), ("unfused_attention", C.c_int32),
+                ("persistent_decode", C.c_int32)]
 
 
 P = C.c_void_p
@@ -132,6 +133,8 @@ _SIGS = {
     "amcu_attn_prefill": (C.c_int, [C.POINTER(AmcuAttentionArgs), P]),
     "amcu_attn_decode_noalloc": (C.c_int, [C.POINTER(AmcuAttentionArgs), P]),
     "amcu_attn_decode_rope": (C.c_int, [C.POINTER(AmcuRopeKvArgs), C.POINTER(AmcuAttentionArgs), P]),
+    "amcu_decode_stack": (C.c_int, [P, P]),
+    "amcu_decode_stack_workspace_bytes": (C.c_size_t, [P]),
     "amcu_silu_mul": (C.c_int, [P, P, P, C.c_int64, C.c_int32, P]),
     "amcu_add": (C.c_int, [P, P, P, C.c_int64, C.c_int32, P]),
     "amcu_argmax": (C.c_int, [P, C.c_int64, C.c_int64, C.c_int64, C.c_int32, P, P, P]),

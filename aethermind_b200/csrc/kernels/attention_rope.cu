@@ -47,7 +47,6 @@ struct RopeAttnParams {
 
 template <int GRP, int D, int CS>
 __global__ void __launch_bounds__(kRaThreads) attn_rope_decode_kernel(RopeAttnParams p) {
-    constexpr int HALF = D / 2;
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int kvh = blockIdx.y;
@@ -82,39 +81,11 @@ __global__ void __launch_bounds__(kRaThreads) attn_rope_decode_kernel(RopeAttnPa
     __shared__ float pm[GRP], pl[GRP];
     __shared__ float po[GRP][D];
 
-    auto angle = [&](int i, float& c, float& s) {
-        if (p.cos_sin) {
-            const float2 v = reinterpret_cast<const float2*>(p.cos_sin)[pos * HALF + i];
-            c = v.x;
-            s = v.y;
-        } else {
-            rope_angle(p.theta, D, pos, i, c, s);
-        }
-    };
-    // query heads kvh*GRP .. kvh*GRP + GRP - 1, rotated and rounded to bf16
-    const __nv_bfloat16* qrow = p.q + row * p.q_stride + (int64_t)kvh * GRP * D;
-    for (int i = threadIdx.x; i < GRP * HALF; i += kRaThreads) {
-        const int h = i / HALF, j = i % HALF;
-        float c, s;
-        angle(j, c, s);
-        const float x1 = __bfloat162float(qrow[h * D + j]), x2 = __bfloat162float(qrow[h * D + j + HALF]);
-        const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-        const float o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
-        qs[h][j] = Act<__nv_bfloat16>::round(o1) * p.scale_log2;
-        qs[h][j + HALF] = Act<__nv_bfloat16>::round(o2) * p.scale_log2;
-    }
-    if (k_begin <= pos && pos < k_end) {  // this CTA's chunk holds the new token: append it
-        const __nv_bfloat16* krow = p.k + row * p.k_stride + (int64_t)kvh * D;
-        const __nv_bfloat16* vrow = p.v + row * p.v_stride + (int64_t)kvh * D;
-        for (int j = threadIdx.x; j < HALF; j += kRaThreads) {
-            float c, s;
-            angle(j, c, s);
-            const float x1 = __bfloat162float(krow[j]), x2 = __bfloat162float(krow[j + HALF]);
-            kbase[pos * D + j] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
-            kbase[pos * D + j + HALF] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
-        }
-        for (int j = threadIdx.x; j < D; j += kRaThreads) vbase[pos * D + j] = vrow[j];
-    }
+    rope_stage_q<GRP, D>(p.q + row * p.q_stride + (int64_t)kvh * GRP * D, pos, p.cos_sin, p.theta, p.scale_log2, qs,
+                         threadIdx.x, kRaThreads);
+    if (k_begin <= pos && pos < k_end)  // this CTA's chunk holds the new token: append it
+        rope_append_kv<D>(p.k + row * p.k_stride + (int64_t)kvh * D, p.v + row * p.v_stride + (int64_t)kvh * D,
+                          kbase + pos * D, vbase + pos * D, pos, p.cos_sin, p.theta, threadIdx.x, kRaThreads);
     __syncthreads();  // q staged; the appended row is visible to this CTA's reads
 
     DecodeWarpState<GRP, D> st;

@@ -197,4 +197,60 @@ __device__ __forceinline__ void decode_merge_warps(int h, int dd, const float (*
     }
 }
 
+// cos/sin of RoPE pair i at position pos: the session table when given, else
+// the double-precision formula (the same values).
+template <int D>
+__device__ __forceinline__ void rope_cs(const float* cos_sin, double theta, int64_t pos, int i, float& c, float& s) {
+    if (cos_sin) {
+        const float2 v = reinterpret_cast<const float2*>(cos_sin)[pos * (D / 2) + i];
+        c = v.x;
+        s = v.y;
+    } else {
+        rope_angle(theta, D, pos, i, c, s);
+    }
+}
+
+// The GRP query heads at qrow, rotated at pos, rounded to bf16 as the
+// in-place RoPE store rounds them, times scale_log2, into qs. Threads
+// tid = 0 .. nthreads - 1 share the work.
+template <int GRP, int D, bool CG = false>
+__device__ __forceinline__ void rope_stage_q(const __nv_bfloat16* qrow, int64_t pos, const float* cos_sin, double theta,
+                                             float scale_log2, float (*qs)[D], int tid, int nthreads) {
+    constexpr int HALF = D / 2;
+    auto ld = [](const __nv_bfloat16* ptr) {
+        if constexpr (CG) return __ldcg(ptr);
+        else return *ptr;
+    };
+    for (int i = tid; i < GRP * HALF; i += nthreads) {
+        const int h = i / HALF, j = i % HALF;
+        float c, s;
+        rope_cs<D>(cos_sin, theta, pos, j, c, s);
+        const float x1 = __bfloat162float(ld(qrow + h * D + j)), x2 = __bfloat162float(ld(qrow + h * D + j + HALF));
+        const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        const float o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+        qs[h][j] = Act<__nv_bfloat16>::round(o1) * scale_log2;
+        qs[h][j + HALF] = Act<__nv_bfloat16>::round(o2) * scale_log2;
+    }
+}
+
+// Appends one token of one kv head: k rotated at pos into kdst, v copied.
+template <int D, bool CG = false>
+__device__ __forceinline__ void rope_append_kv(const __nv_bfloat16* krow, const __nv_bfloat16* vrow,
+                                               __nv_bfloat16* kdst, __nv_bfloat16* vdst, int64_t pos,
+                                               const float* cos_sin, double theta, int tid, int nthreads) {
+    constexpr int HALF = D / 2;
+    auto ld = [](const __nv_bfloat16* ptr) {
+        if constexpr (CG) return __ldcg(ptr);
+        else return *ptr;
+    };
+    for (int j = tid; j < HALF; j += nthreads) {
+        float c, s;
+        rope_cs<D>(cos_sin, theta, pos, j, c, s);
+        const float x1 = __bfloat162float(ld(krow + j)), x2 = __bfloat162float(ld(krow + j + HALF));
+        kdst[j] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
+        kdst[j + HALF] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
+    }
+    for (int j = tid; j < D; j += nthreads) vdst[j] = ld(vrow + j);
+}
+
 }  // namespace amcu

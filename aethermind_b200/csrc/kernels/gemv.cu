@@ -27,39 +27,10 @@
 #include "../amcu_internal.h"
 #include "common.cuh"
 #include "gemv.cuh"
+#include "gemv_stage.cuh"
+#include "mma_int4.cuh"
 
 namespace amcu {
-
-__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Four int8 values -> two bf16x2 (bytes 0,1) and (bytes 2,3); exact.
-__device__ __forceinline__ void unpack_w8_word(uint32_t w, uint32_t& lo, uint32_t& hi) {
-    const uint32_t u = w ^ 0x80808080u;  // offset binary: q + 128
-    float f[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t bits = __byte_perm(u, 0x4B000000u, 0x7650u + i);  // 0x4B0000bb = 2^23 + bb
-        f[i] = __uint_as_float(bits) - 8388736.0f;                      // - (2^23 + 128)
-    }
-    __nv_bfloat162 p0 = __floats2bfloat162_rn(f[0], f[1]);
-    __nv_bfloat162 p1 = __floats2bfloat162_rn(f[2], f[3]);
-    lo = *reinterpret_cast<uint32_t*>(&p0);
-    hi = *reinterpret_cast<uint32_t*>(&p1);
-}
 
 template <typename T>
 __device__ __forceinline__ T epi_store(float v) { return Act<T>::store(v); }
@@ -145,17 +116,6 @@ constexpr int kXPad = 16;  // bytes of padding per staged activation row
 #define GEMV_CPS 2
 #endif
 
-// INT4 word -> fp16 MMA registers: a0/a2 = 1032 + q (bits 0-3, 8-11 of each
-// half: rows g), a1/a3 = 1152 + 16q (bits 4-7, 12-15: rows g+8). (w & mask)
-// ^ c flips the nibble's sign bit (n ^ 8 = q + 8) and sets exponent 1024.
-__device__ __forceinline__ void unpack_w4_word_f16(uint32_t w, uint32_t (&a)[4]) {
-    const uint32_t w8 = w >> 8;
-    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(a[0]) : "r"(w), "r"(0x000F000Fu), "r"(0x64086408u));
-    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(a[1]) : "r"(w), "r"(0x00F000F0u), "r"(0x64806480u));
-    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(a[2]) : "r"(w8), "r"(0x000F000Fu), "r"(0x64086408u));
-    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(a[3]) : "r"(w8), "r"(0x00F000F0u), "r"(0x64806480u));
-}
-
 // Shared memory carve-up (bytes; every part 128-byte aligned).
 struct GemvSmem {
     int red, sx, xs, ring, bars, total;
@@ -235,162 +195,16 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
     pdl_wait();
     pdl_trigger();
 
-    // ---- stage the activations [m][k] (+16 B per row): copy, RMSNorm factors
-    // (fused norm), then for INT4 one pass that normalizes, converts to fp16
-    // and sums every 128-column group.
+    // ---- stage the activations (fused RMSNorm; INT4: fp16 + group sums)
+    __shared__ StageShared stsh;
+    {
+        StageCtx sc{static_cast<const __nv_bfloat16*>(p.x), p.x_stride, p.k, M,
+                    static_cast<const __nv_bfloat16*>(p.norm_w), p.eps, xs, xrow, sx, &stsh,
+                    (int)threadIdx.x, kGemvConsumers * 32, 2};
+        stage_activations<W4>(sc);
+    }
+    const float* row_mul = stsh.row_mul;
     constexpr int NT = kGemvConsumers * 32;
-    __shared__ float row_mul[kGemvMaxM];  // epilogue multiplier per activation row (a power of two)
-    __shared__ float row_inv[kGemvMaxM];  // RMSNorm factor per row
-    __shared__ unsigned int row_big;      // bit m: row m needs a multiplier above 1 (fp16 overflow guard)
-    const int chunks = (int)(p.k / 8);    // 16-byte chunks per row
-    const __nv_bfloat16* xg = static_cast<const __nv_bfloat16*>(p.x);
-    const __nv_bfloat16* nwt = static_cast<const __nv_bfloat16*>(p.norm_w);
-    if (threadIdx.x < kGemvMaxM) row_mul[threadIdx.x] = 1.f;
-    if (threadIdx.x == 0) row_big = 0u;
-    for (int i = threadIdx.x; i < M * chunks; i += NT) {
-        const int m = i / chunks, c = i - m * chunks;
-        *reinterpret_cast<uint4*>(xs + m * xrow + c * 16) = ld_u4(xg + m * p.x_stride + c * 8);
-    }
-    named_bar_sync(2, NT);
-    if (p.norm_w) {
-        // row m's factor (mean(x^2) + eps)^-1/2, reduced by warp m % 8 in a
-        // fixed order; y = round(x * factor * w) as the RMSNorm kernel computes it
-        for (int m = warp; m < M; m += kGemvConsumers) {
-            const uint8_t* xr = xs + m * xrow;
-            float ss = 0.f;
-            for (int c = lane; c < chunks; c += 32) {
-                const uint4 v = *reinterpret_cast<const uint4*>(xr + c * 16);
-                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float a = __uint_as_float(w4[j] << 16), b = __uint_as_float(w4[j] & 0xffff0000u);
-                    ss += a * a + b * b;
-                }
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) row_inv[m] = 1.0f / sqrtf(ss / (float)p.k + p.eps);
-        }
-        named_bar_sync(2, NT);
-    }
-    // normalized bf16 value of element pair j of a 16-byte chunk (a: x bits, w: norm weight bits)
-    auto norm2 = [&](uint32_t a, uint32_t w, float inv, float& lo, float& hi) {
-        lo = __uint_as_float(a << 16);
-        hi = __uint_as_float(a & 0xffff0000u);
-        if (p.norm_w) {
-            lo = Act<__nv_bfloat16>::round(lo * inv * __uint_as_float(w << 16));
-            hi = Act<__nv_bfloat16>::round(hi * inv * __uint_as_float(w & 0xffff0000u));
-        }
-    };
-    if constexpr (W4) {
-        // one thread per 16-column segment (8 per group): normalize, convert
-        // to fp16 (times 1/row_mul), sum; the group sum is a shuffle over the
-        // segment's 8 lanes
-        auto convert_pass = [&](bool redo) {
-            const int segs = G * 8 * M;
-            for (int s0 = 0; s0 < segs; s0 += NT) {
-                const int s = s0 + threadIdx.x;
-                float sum = 0.f;
-                int m = 0, grp = 0;
-                bool active = s < segs;
-                if (active) {
-                    m = s / (G * 8);
-                    const int r = s - m * G * 8;
-                    grp = r >> 3;
-                    active = !redo || ((row_big >> m) & 1u);
-                    if (active) {
-                        const int c0 = grp * 16 + (r & 7) * 2;  // first 16-byte chunk of the segment
-                        uint4* xp = reinterpret_cast<uint4*>(xs + m * xrow + c0 * 16);
-                        uint4 v[2], wv[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-                        if (redo) {
-                            v[0] = ld_u4(xg + m * p.x_stride + c0 * 8);
-                            v[1] = ld_u4(xg + m * p.x_stride + c0 * 8 + 8);
-                        } else {
-                            v[0] = xp[0];
-                            v[1] = xp[1];
-                        }
-                        if (p.norm_w) {
-                            wv[0] = ld_u4(nwt + c0 * 8);
-                            wv[1] = ld_u4(nwt + c0 * 8 + 8);
-                        }
-                        const float inv = p.norm_w ? row_inv[m] : 1.f, mul = 1.0f / row_mul[m];
-                        const uint32_t a[8] = {v[0].x, v[0].y, v[0].z, v[0].w, v[1].x, v[1].y, v[1].z, v[1].w};
-                        const uint32_t w[8] = {wv[0].x, wv[0].y, wv[0].z, wv[0].w, wv[1].x, wv[1].y, wv[1].z, wv[1].w};
-                        uint32_t h[8];
-                        float amax = 0.f;
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            float lo, hi;
-                            norm2(a[j], w[j], inv, lo, hi);
-                            amax = fmaxf(amax, fmaxf(fabsf(lo), fabsf(hi)));
-                            const __half2 hv = __floats2half2_rn(lo * mul, hi * mul);
-                            sum += __low2float(hv) + __high2float(hv);
-                            h[j] = *reinterpret_cast<const uint32_t*>(&hv);
-                        }
-                        if (!redo && amax > 32768.f) atomicOr(&row_big, 1u << m);
-                        xp[0] = make_uint4(h[0], h[1], h[2], h[3]);
-                        xp[1] = make_uint4(h[4], h[5], h[6], h[7]);
-                    }
-                }
-                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-                if (active && (s & 7) == 0) sx[grp * 8 + m] = sum;
-            }
-        };
-        convert_pass(false);
-        for (int i = threadIdx.x; i < G * 8; i += NT)
-            if ((i & 7) >= M) sx[i] = 0.f;  // rows without activations add nothing
-        named_bar_sync(2, NT);
-        if (row_big != 0u) {
-            // Rare: a row reaches 2^15, beyond what fp16 staging keeps. Find
-            // its max, stage it again times 2^-e (exact) and let the epilogue
-            // multiply by 2^e.
-            __shared__ unsigned int row_amax[kGemvMaxM];
-            if (threadIdx.x < kGemvMaxM) row_amax[threadIdx.x] = 0u;
-            named_bar_sync(2, NT);
-            for (int i = threadIdx.x; i < M * chunks; i += NT) {
-                const int m = i / chunks, c = i - m * chunks;
-                if (!((row_big >> m) & 1u)) continue;
-                const uint4 v = ld_u4(xg + m * p.x_stride + c * 8);
-                const uint4 wv = p.norm_w ? ld_u4(nwt + c * 8) : make_uint4(0, 0, 0, 0);
-                const uint32_t a[4] = {v.x, v.y, v.z, v.w}, w[4] = {wv.x, wv.y, wv.z, wv.w};
-                float amax = 0.f;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float lo, hi;
-                    norm2(a[j], w[j], p.norm_w ? row_inv[m] : 1.f, lo, hi);
-                    amax = fmaxf(amax, fmaxf(fabsf(lo), fabsf(hi)));
-                }
-                atomicMax(&row_amax[m], __float_as_uint(amax));
-            }
-            named_bar_sync(2, NT);
-            if (threadIdx.x < M && ((row_big >> threadIdx.x) & 1u)) {
-                // e = exponent(max) - 14 keeps the scaled max below 2^15
-                const int e = (int)((row_amax[threadIdx.x] >> 23) & 0xff) - 127 - 14;
-                row_mul[threadIdx.x] = __int_as_float((127 + (e > 0 ? e : 0)) << 23);
-            }
-            named_bar_sync(2, NT);
-            convert_pass(true);
-            named_bar_sync(2, NT);
-        }
-    } else if (p.norm_w) {
-        for (int i = threadIdx.x; i < M * chunks; i += NT) {
-            const int m = i / chunks, c = i - m * chunks;
-            uint4* xp = reinterpret_cast<uint4*>(xs + m * xrow + c * 16);
-            const uint4 v = *xp, wv = ld_u4(nwt + c * 8);
-            const uint32_t a[4] = {v.x, v.y, v.z, v.w}, w[4] = {wv.x, wv.y, wv.z, wv.w};
-            uint32_t o[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float lo, hi;
-                norm2(a[j], w[j], row_inv[m], lo, hi);
-                __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
-                o[j] = *reinterpret_cast<uint32_t*>(&h2);
-            }
-            *xp = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-        named_bar_sync(2, NT);
-    }
     const float rm0 = 2 * t < M ? row_mul[2 * t] : 1.f, rm1 = 2 * t + 1 < M ? row_mul[2 * t + 1] : 1.f;
 
     // Lanes whose activation row does not exist (g >= M) read row 0: they only

@@ -9,6 +9,8 @@
 //   RoPE + KVCacheUpdate   -> kRoPE (rotates q, writes rotated k and v to the cache)
 //   RoPE + KVCacheUpdate + Attention (decode, bf16)
 //                          -> kRoPEAttention (one launch, rotated q stays on chip)
+//   every decoder layer of a bs <= 2 INT4 decode step
+//                          -> kDecodeStack (one persistent cooperative launch)
 //   o Linear + Add         -> kLinear with the residual-add epilogue
 //   gate/up Linear+SiluMul -> kLinear over the interleaved gate/up weight (SiLU-Mul epilogue)
 //   down Linear + Add      -> kLinear with the residual-add epilogue
@@ -243,6 +245,17 @@ Status RopeAttnFn(const KernelContext& c) noexcept {
     return FromAm(amcu_attn_decode_rope(&a->rope, &a->attn, S(c)));
 }
 
+// ---- persistent decode step (attrs: the complete AmcuDecodeStackArgs) ----
+Status BuildDecodeStack(std::span<const TensorView>, std::span<const MutableTensorView>,
+                        std::span<const std::byte> attrs, const void*, void* buf) noexcept {
+    if (attrs.size() != sizeof(AmcuDecodeStackArgs)) return Status::InvalidArgument("DecodeStack attrs missing");
+    std::memcpy(buf, attrs.data(), sizeof(AmcuDecodeStackArgs));
+    return Status::Ok();
+}
+Status DecodeStackFn(const KernelContext& c) noexcept {
+    return FromAm(amcu_decode_stack(static_cast<const AmcuDecodeStackArgs*>(c.kernel_params), S(c)));
+}
+
 // ---- elementwise ----
 struct BinaryArgs {
     const void* a;
@@ -367,6 +380,10 @@ AM_REGISTER_KERNEL(Attn_CUDA_BF16_Prefill, KernelDescriptor{OpType::kAttention, 
 AM_REGISTER_KERNEL(RoPEAttn_CUDA_BF16_Decode,
                    KernelDescriptor{OpType::kRoPEAttention, AM_SEL(kBF16, kBF16, kPlain, kDecode), RopeAttnFn,
                                     "RoPEAttnDecodeCluster_CUDA_BF16", 0, BuildRopeAttention, sizeof(RopeAttnArgs)})
+
+AM_REGISTER_KERNEL(DecodeStack_CUDA_W4,
+                   KernelDescriptor{OpType::kDecodeStack, AM_SEL(kBF16, kI4, kQuantizedInt4, kDecode), DecodeStackFn,
+                                    "DecodeStackPersistent_CUDA_W4", 0, BuildDecodeStack, sizeof(AmcuDecodeStackArgs)})
 
 AM_REGISTER_KERNEL(SiluMul_CUDA_F32, KernelDescriptor{OpType::kSiluMul, AM_SEL(kF32, kF32, kPlain, kBoth), SiluMulFn,
                                                       "SiluMul_CUDA_F32", 0, BuildBinary, sizeof(BinaryArgs)})

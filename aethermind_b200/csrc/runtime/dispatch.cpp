@@ -35,6 +35,7 @@ const char* ToString(OpType op) noexcept {
         case OpType::kPermute: return "Permute";
         case OpType::kReorder: return "Reorder";
         case OpType::kRoPEAttention: return "RoPEAttention";
+        case OpType::kDecodeStack: return "DecodeStack";
         default: return "Unknown";
     }
 }

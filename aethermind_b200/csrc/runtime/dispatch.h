@@ -45,6 +45,7 @@ enum class OpType : uint16_t {
     kPermute,
     kReorder,
     kRoPEAttention,  // fused decode step: RoPE + KVCacheUpdate + Attention
+    kDecodeStack,    // persistent decode step: every decoder layer in one launch
 };
 const char* ToString(OpType op) noexcept;
 

@@ -306,6 +306,10 @@ struct am_session_s {
     aethermind::DeviceBuffer tokens, next_tok, seq_pos, counter, out_tokens, gaps, gap_tmp, status;
     aethermind::DeviceBuffer x, h, qkv, attn, act, part, hlast, logits;
     aethermind::DeviceBuffer rope_table;  // [max_seq][head_dim/2] (cos, sin)
+    // persistent decode step: per-layer descriptor table and its workspace
+    // (zeroed once; its counters reset themselves after every launch)
+    aethermind::DeviceBuffer stack_layers, stack_ws;
+    bool graph_unsupported = false;  // decode plan could not be captured: eager decode
     int64_t rows_cap = 0, out_cap = 0;
     // plans
     aethermind::ExecutionPlan prefill, decode;
@@ -476,7 +480,54 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
                                   {ids, table}, {MView2(s->x.data(), A, M, H, H)}, &ea, nullptr, "embedding"));
     }
     RmsNormAttrs na{c.rms_eps};
-    for (int64_t l = 0; l < c.layers; ++l) {
+    // Decode of a bs <= 2 INT4 model on one GPU: every decoder layer in one
+    // persistent launch (amcu_decode_stack), when the session asks for it.
+    const KernelSelector stack_sel = pb.Sel(A, DType::kI4, WeightFormat::kQuantizedInt4);
+    const bool use_stack = phase == ExecPhase::kDecode && R == 1 && B <= 2 && !tp &&
+                           wf == WeightFormat::kQuantizedInt4 && A == DType::kBF16 &&
+                           s->cfg.persistent_decode != 0 && c.hidden % 2048 == 0 && m->inter_l % 2048 == 0 &&
+                           (m->nq_l * d) % 2048 == 0 && m->rt->backend->ResolveKernelInfo(OpType::kDecodeStack, stack_sel).ok();
+    if (use_stack) {
+        std::vector<AmcuDecodeLayer> tab(c.layers);
+        for (int64_t l = 0; l < c.layers; ++l) {
+            auto& L = m->layers[l];
+            tab[l] = AmcuDecodeLayer{L.qkv.w.data, L.o.w.data, L.gu.w.data, L.d.w.data, L.attn_norm.data(),
+                                     L.mlp_norm.data(), s->kv.key_plane(l), s->kv.value_plane(l)};
+        }
+        if (!s->stack_layers.is_initialized() || s->stack_layers.size() < tab.size() * sizeof(AmcuDecodeLayer))
+            AM_RETURN_IF_ERROR(AllocVec(m, s->stack_layers, tab.size() * sizeof(AmcuDecodeLayer)));
+        AM_CUDA(UploadSync(m, s->stack_layers.data(), tab.data(), tab.size() * sizeof(AmcuDecodeLayer)));
+        AmcuDecodeStackArgs a{};
+        a.layers = static_cast<const AmcuDecodeLayer*>(s->stack_layers.data());
+        a.n_layers = c.layers;
+        a.batch = B;
+        a.hidden = H;
+        a.inter = m->inter_l;
+        a.n_q_heads = m->nq_l;
+        a.n_kv_heads = m->nkv_l;
+        a.head_dim = d;
+        a.x = s->x.data();
+        a.qkv = s->qkv.data();
+        a.attn = s->attn.data();
+        a.act = s->act.data();
+        a.seq_pos = s->seq_pos.as<int32_t>();
+        a.capacity = (int64_t)s->kv.layout().max_tokens;
+        a.slot_stride = (int64_t)(s->kv.layout().slot_stride / e);
+        a.cos_sin = s->rope_table.as<float>();
+        a.theta = c.rope_theta;
+        a.rms_eps = c.rms_eps;
+        a.status = s->status.as<int32_t>();
+        const size_t wsb = amcu_decode_stack_workspace_bytes(&a);
+        if (!s->stack_ws.is_initialized() || s->stack_ws.size() < wsb) {
+            AM_RETURN_IF_ERROR(AllocVec(m, s->stack_ws, wsb));
+            AM_CUDA(cudaMemsetAsync(s->stack_ws.data(), 0, wsb, m->rt->stream));
+            AM_CUDA(cudaStreamSynchronize(m->rt->stream));
+        }
+        a.workspace = s->stack_ws.data();
+        a.workspace_size = s->stack_ws.size();
+        AM_RETURN_IF_ERROR(pb.Add(OpType::kDecodeStack, stack_sel, {}, {}, &a, nullptr, "decoder_layers (persistent)", true));
+    }
+    for (int64_t l = 0; l < (use_stack ? 0 : c.layers); ++l) {
         auto& L = m->layers[l];
         const std::string p = "layer" + std::to_string(l) + ".";
         LinearAttrs store{AMCU_EPI_STORE};
@@ -655,7 +706,7 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
     // token counter the prefill's last kernel wrote.
     AM_CUDA(cudaStreamSynchronize(st));
 
-    const bool use_graph = s->cfg.use_cuda_graph != 0;
+    bool use_graph = s->cfg.use_cuda_graph != 0 && !s->graph_unsupported;
     range.reset();
     range = std::make_unique<NvtxRange>("am_decode");
     for (int64_t i = 1; i < N; ++i) {
@@ -675,12 +726,18 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
             Status cs = s->exec.Execute(s->decode, stream, &s->ws, &kv);
             if (cs.ok()) cs = RunAdvance(s, B, -1, st);
             cudaError_t ce = cudaStreamEndCapture(st, &g);
-            AM_RETURN_IF_ERROR(cs);
-            AM_CUDA(ce);
             cudaGraphExec_t ge = nullptr;
-            cudaError_t ie = cudaGraphInstantiate(&ge, g, 0);
-            cudaGraphDestroy(g);
-            AM_CUDA(ie);
+            cudaError_t ie = cudaErrorInvalidValue;
+            if (cs.ok() && ce == cudaSuccess) ie = cudaGraphInstantiate(&ge, g, 0);
+            if (g) cudaGraphDestroy(g);
+            if (!cs.ok() || ce != cudaSuccess || ie != cudaSuccess) {
+                // A step of this plan cannot be captured: this session decodes
+                // eagerly from now on (the captured steps never ran).
+                cudaGetLastError();
+                s->graph_unsupported = true;
+                use_graph = false;
+                continue;
+            }
             s->graph = ge;
             s->graph_B = B;
             AM_CUDA(cudaGraphUpload(ge, st));

@@ -126,11 +126,12 @@ class Model:
 
 class Session:
     def __init__(self, model: Model, max_new_tokens: int = 0, use_cuda_graph: bool = True,
-                 fused_attention: bool = True):
+                 fused_attention: bool = True, persistent_decode: bool = False):
         self.model = model
         c = L.AmSessionConfig()
         c.max_new_tokens, c.use_cuda_graph = max_new_tokens, int(use_cuda_graph)
         c.unfused_attention = 0 if fused_attention else 1
+        c.persistent_decode = 1 if persistent_decode else 0
         h = lib().am_session_create(model.h, C.byref(c))
         if not h:
             raise _err("am_session_create")

@@ -295,6 +295,46 @@ typedef struct AmcuAttentionArgs {
 } AmcuAttentionArgs;
 size_t amcu_attention_workspace_bytes(const AmcuAttentionArgs* args);
 am_status_code amcu_attn_decode(const AmcuAttentionArgs* args, void* stream);
+/* ------------------------------------------------------------------------ */
+/* Persistent decode step (no single counterpart in the reference: it runs  */
+/* every decoder layer of BuildLlamaDense -- attention RMSNorm, q/k/v        */
+/* Linear, RoPE, KVCacheUpdate, Attention, o Linear + Add, MLP RMSNorm,      */
+/* gate/up Linear + SiluMul, down Linear + Add -- for one decode step of a   */
+/* bs <= 2, INT4 g128, bf16 model in one cooperative launch; one CTA per SM   */
+/* streams its share of every layer's weights without pausing at the layer   */
+/* or phase boundaries).                                                      */
+/* ------------------------------------------------------------------------ */
+typedef struct AmcuDecodeLayer {   /* one decoder layer, device pointers */
+    const void* w_qkv;             /* INT4 [(nq + 2 nkv) * head_dim][hidden], device format */
+    const void* w_o;               /* INT4 [hidden][nq * head_dim] */
+    const void* w_gate_up;         /* INT4 [2 inter][hidden] from amcu_prepack_gate_up */
+    const void* w_down;            /* INT4 [hidden][inter] */
+    const void* attn_norm;         /* bf16 [hidden] */
+    const void* mlp_norm;          /* bf16 [hidden] */
+    void* k_cache;                 /* this layer's K plane [slots][nkv][capacity][head_dim] */
+    void* v_cache;
+} AmcuDecodeLayer;
+typedef struct AmcuDecodeStackArgs {
+    const AmcuDecodeLayer* layers; /* device array of n_layers descriptors */
+    int64_t n_layers;
+    int64_t batch;                 /* sequences (one row each), 1 or 2 */
+    int64_t hidden, inter, n_q_heads, n_kv_heads, head_dim;
+    void* x;                       /* [batch][hidden] bf16 residual stream, updated in place */
+    void* qkv;                     /* [batch][(nq + 2 nkv) * head_dim] bf16 scratch */
+    void* attn;                    /* [batch][nq * head_dim] bf16 scratch */
+    void* act;                     /* [batch][inter] bf16 scratch */
+    const int32_t* seq_pos;        /* [batch] position of each sequence's token */
+    int64_t capacity, slot_stride; /* KV cache (slot_stride 0: n_kv * capacity * head_dim) */
+    const float* cos_sin;          /* optional amcu_rope_table table */
+    double theta;
+    float rms_eps;
+    int32_t* status;               /* optional: AM_STATUS_OUT_OF_RANGE on a position >= capacity */
+    void* workspace;               /* amcu_decode_stack_workspace_bytes, 256-byte aligned, ZERO before the */
+    size_t workspace_size;         /* first call (its counters reset themselves after every call) */
+} AmcuDecodeStackArgs;
+size_t amcu_decode_stack_workspace_bytes(const AmcuDecodeStackArgs* args);
+am_status_code amcu_decode_stack(const AmcuDecodeStackArgs* args, void* stream);
+
 /* Fused decode step: amcu_rope_kv_write(rope) then amcu_attn_decode(attn) in
  * one launch (bf16, one row per sequence; attn->q == rope->q, same caches and
  * positions). The rotated q is used on chip and NOT written back to rope->q;
@@ -394,6 +434,8 @@ typedef struct am_session_config_t {
     int32_t use_cuda_graph;  /* 1: decode steps replay a captured CUDA graph */
     int32_t unfused_attention; /* 1: decode RoPE and attention as two launches (default 0: one fused
                                   launch, amcu_attn_decode_rope, where the dtype has one) */
+    int32_t persistent_decode; /* 1: all decoder layers of a bs <= 2 INT4 decode step in one persistent
+                                  launch (amcu_decode_stack); default 0: one launch per op, faster today */
 } am_session_config_t;
 
 am_runtime_t am_runtime_create(const am_config_t* config);

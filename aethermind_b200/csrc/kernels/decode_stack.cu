@@ -28,7 +28,9 @@
 // The kernel is launched cooperatively (all CTAs co-resident or no launch).
 #include <cooperative_groups.h>
 
+#include <cstdio>
 #include <cstdlib>
+#include <vector>
 
 #include "../amcu_internal.h"
 #include "attn_decode.cuh"
@@ -62,12 +64,26 @@ struct DsParams {
     float eps, scale_log2;
     float* attn_ws;               // [B][nkv][ns][GRP][D + 2]
     int32_t* attn_cnt;            // [B][nkv] arrivals (zero between uses)
-    unsigned int* bar;            // [2] grid barrier: count, generation (zero between uses)
+    unsigned int* bar;            // grid barrier words (zero between uses)
     int ns;                       // attention splits per (sequence, kv head)
     int stages;
     int32_t *err, *status;
-    int dbg_skip;  // diagnostics (AMCU_DS_SKIP): bit 0 skips attention, bit 1 the grid barriers (wrong results)
+    int rbmax;     // most row blocks a CTA owns in any GEMV phase
+    int dbg_skip;  // diagnostics (AMCU_DS_SKIP): bit 0 skips attention, bit 1 the grid barriers, bit 2 the weight stream (wrong results)
+    unsigned long long* trace;  // diagnostics (AMCU_DS_TRACE): [cta][layer][kDsMarks] globaltimer stamps, or null
 };
+
+constexpr int kDsMarks = 26;  // trace stamps per layer
+
+__device__ __forceinline__ void ds_mark(const DsParams& p, int l, int idx) {
+    if (p.trace && threadIdx.x == 0) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        p.trace[((size_t)blockIdx.x * p.nlayers + l) * kDsMarks + idx] = t;
+        if (idx == 0 || idx == 18)  // SM clock cycles beside the layer's first and last stamps
+            p.trace[((size_t)blockIdx.x * p.nlayers + l) * kDsMarks + (idx == 0 ? 24 : 25)] = clock64();
+    }
+}
 
 // Row blocks [lo, hi) of an n-row weight that CTA c of `ctas` handles.
 __device__ __forceinline__ void ds_range(int64_t n, int c, int ctas, int& lo, int& hi) {
@@ -76,23 +92,51 @@ __device__ __forceinline__ void ds_range(int64_t n, int c, int ctas, int& lo, in
     hi = (int)(nrb * (c + 1) / ctas);
 }
 
-// Consumer-side grid barrier: thread 0 arrives and spins (bounded) on the
-// generation word, then the consumer threads meet.
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* a) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* a, unsigned int v) {
+    unsigned int old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void st_relaxed_gpu(unsigned int* a, unsigned int v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+
+// Consumer-side grid barrier, two levels: after the consumer threads meet,
+// thread 0 arrives (release) on its group's counter (CTA % kDsBarGroups,
+// each counter in its own 128-byte line); the last arrival of a group
+// arrives on the top counter, and the last arrival there resets it and bumps
+// the generation word, on which everyone else spins with acquire loads
+// (bounded). Counters return to zero before the generation moves.
+constexpr int kDsBarGroups = 16;
+constexpr int kDsBarWords = 32 * (2 + kDsBarGroups);  // gen, top, groups: one 128-byte line each
 __device__ __forceinline__ void ds_grid_barrier(const DsParams& p, bool& ok) {
     if (p.dbg_skip & 2) return;
     named_bar_sync(kBarGemv, kDsCT);
     if (threadIdx.x == 0) {
-        volatile unsigned int* gen = p.bar + 1;
-        const unsigned int g0 = *gen;
-        __threadfence();
-        const unsigned int arrived = atomicAdd(p.bar, 1u);
-        if (arrived == gridDim.x - 1) {
-            p.bar[0] = 0u;
-            __threadfence();
-            atomicAdd(p.bar + 1, 1u);
-        } else if (ok) {
+        unsigned int* gen = p.bar;
+        unsigned int* top = p.bar + 32;
+        const int grp = blockIdx.x % kDsBarGroups;
+        const int ngrp = (int)gridDim.x < kDsBarGroups ? (int)gridDim.x : kDsBarGroups;
+        const unsigned int members = (gridDim.x - grp + kDsBarGroups - 1) / kDsBarGroups;
+        unsigned int* cnt = p.bar + 64 + 32 * grp;
+        const unsigned int g0 = ld_acquire_gpu(gen);
+        bool released = false;
+        if (atom_add_acq_rel_gpu(cnt, 1u) == members - 1) {
+            st_relaxed_gpu(cnt, 0u);
+            if (atom_add_acq_rel_gpu(top, 1u) == (unsigned int)ngrp - 1) {
+                st_relaxed_gpu(top, 0u);
+                atom_add_acq_rel_gpu(gen, 1u);
+                released = true;
+            }
+        }
+        if (!released && ok) {
             const long long t0 = clock64();
-            while (*gen == g0) {
+            while (ld_acquire_gpu(gen) == g0) {
                 if (clock64() - t0 > kSpinLimitCycles) {
                     record_device_error(p.err, kErrDsBarrier);
                     ok = false;
@@ -100,16 +144,23 @@ __device__ __forceinline__ void ds_grid_barrier(const DsParams& p, bool& ok) {
                 }
             }
         }
-        __threadfence();
     }
     named_bar_sync(kBarGemv, kDsCT);
+}
+
+// L2 prefetch of a small read-only array (a norm weight) a phase before its
+// use, so the staging after the next grid barrier does not wait on HBM.
+__device__ __forceinline__ void ds_prefetch_l2(const void* ptr, int64_t bytes) {
+    if (blockIdx.x != 0 || ptr == nullptr) return;
+    for (int64_t off = (int64_t)threadIdx.x * 128; off < bytes; off += (int64_t)kDsCT * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(static_cast<const char*>(ptr) + off));
 }
 
 struct DsSmem {
     int ring, bars, red, sx, un, total;
 };
 template <int GRP, int D>
-__host__ __device__ inline DsSmem ds_smem(int64_t kmax, int stages) {
+__host__ __device__ inline DsSmem ds_smem(int64_t kmax, int stages, int rbmax) {
     auto up = [](int64_t v) { return (int)((v + 127) / 128 * 128); };
     const int64_t xs = kDsMaxRows * (kmax * 2 + 16);
     const int64_t att = (int64_t)GRP * D * 4 + 2 * kDsConsumers * GRP * 4 + (int64_t)kDsConsumers * GRP * D * 4 + 64;
@@ -117,7 +168,7 @@ __host__ __device__ inline DsSmem ds_smem(int64_t kmax, int stages) {
     s.ring = 0;
     s.bars = stages * kDsStageBytes;
     s.red = s.bars + up(2 * stages * 8);
-    s.sx = s.red + 2 * kDsConsumers * 32 * 16;
+    s.sx = s.red + up((int64_t)rbmax * 16 * 8 * 4);  // [rbmax][16 rows][8 activation rows] fp32
     s.un = s.sx + up(kmax / 128 * 8 * 4);
     s.total = s.un + up(xs > att ? xs : att);
     return s;
@@ -136,32 +187,49 @@ struct DsRing {
 template <int EPI>
 __device__ __noinline__ void ds_gemv(const DsParams& p, DsRing& r, int64_t n, int64_t k, const __nv_bfloat16* x,
                         const __nv_bfloat16* norm_w, __nv_bfloat16* y, uint8_t* smem, const DsSmem& L,
-                        StageShared* stsh, bool& ok) {
+                        StageShared* stsh, bool& ok, int l, int m0) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int M = p.B;
     const int xrow = (int)(k * 2 + 16);
     uint8_t* xs = smem + L.un;
     float* sx = reinterpret_cast<float*>(smem + L.sx);
-    float4* red = reinterpret_cast<float4*>(smem + L.red);
+    float* accs = reinterpret_cast<float*>(smem + L.red);
+    {
+        int lo0, hi0;
+        ds_range(n, blockIdx.x, gridDim.x, lo0, hi0);
+        for (int i = threadIdx.x; i < (hi0 - lo0) * 128; i += kDsCT) accs[i] = 0.f;  // staging's barriers publish this
+    }
     {
         StageCtx sc{x, k, k, M, norm_w, p.eps, xs, xrow, sx, stsh, (int)threadIdx.x, kDsCT, kBarStage};
         stage_activations<true, true>(sc);
     }
-    const float rm0 = 2 * t < M ? stsh->row_mul[2 * t] : 1.f, rm1 = 2 * t + 1 < M ? stsh->row_mul[2 * t + 1] : 1.f;
+    ds_mark(p, l, m0);
     const uint8_t* xr = xs + (g < M ? g : 0) * xrow + 32 * t;  // + 256 B per group
     const int per_row = (int)(k / 128) / kDsUnits;
     int lo, hi;
     ds_range(n, blockIdx.x, gridDim.x, lo, hi);
-    int par = 0;
-    for (int rb = lo; rb < hi; ++rb, par ^= 1) {
+    // every warp adds its partial tile of a row block into accs[row block]
+    // (shared-memory float atomics), so no warp waits for another until the
+    // phase's row blocks are all consumed
+    // The ring state and flags live in registers for the loop (the caller's
+    // copies sit in local memory, which every asm memory clobber would reload).
+    const uint8_t* const ring = r.ring + warp * kW4PairBytes;
+    uint64_t* const full = r.full;
+    uint64_t* const empty = r.empty;
+    const int S = r.S;
+    int slot = r.slot;
+    uint32_t phase = r.phase;
+    const bool stream = !(p.dbg_skip & 4);
+    bool live = ok;
+    for (int rb = lo; rb < hi; ++rb) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int j = 0; j < per_row; ++j) {
-            if (ok && !mbar_wait(&r.full[r.slot], r.phase)) {
-                ok = false;
+            if (live && stream && !mbar_wait(&full[slot], phase)) {
+                live = false;
                 if (lane == 0) record_device_error(p.err, kErrDsFull);
             }
-            const uint8_t* rec = r.ring + r.slot * kDsStageBytes + warp * kW4PairBytes;
+            const uint8_t* rec = ring + slot * kDsStageBytes;
             const int grp = j * kDsUnits + warp;
             const uint8_t* xp = xr + grp * 256;
             float part[2][4];
@@ -191,46 +259,44 @@ __device__ __noinline__ void ds_gemv(const DsParams& p, DsRing& r, int64_t n, in
             acc[2] = fmaf(fmaf(-1152.f, s2x.x, part[0][2] + part[1][2]), s_hi, acc[2]);
             acc[3] = fmaf(fmaf(-1152.f, s2x.y, part[0][3] + part[1][3]), s_hi, acc[3]);
             __syncwarp();
-            if (lane == 0) mbar_arrive(&r.empty[r.slot]);
-            if (++r.slot == r.S) {
-                r.slot = 0;
-                r.phase ^= 1;
+            if (lane == 0 && stream) mbar_arrive(&empty[slot]);
+            if (++slot == S) {
+                slot = 0;
+                phase ^= 1;
             }
         }
-        red[(par * kDsConsumers + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        named_bar_sync(kBarGemv, kDsCT);
-        if (warp == rb % kDsConsumers) {
-            float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int w = 0; w < kDsConsumers; ++w) {
-                const float4 v = red[(par * kDsConsumers + w) * 32 + lane];
-                s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
-            }
-            const float v4[4] = {s4.x * rm0, s4.y * rm1, s4.z * rm0, s4.w * rm1};
-            const int m0 = 2 * t, m1 = 2 * t + 1;
-            if constexpr (EPI == AMCU_EPI_SILU_MUL) {
-                // c0/c1: gate row, c2/c3: up row of output column 8*rb + g
-                const int64_t col = (int64_t)rb * 8 + g, ys = n / 2;
-                if (m0 < M)
-                    y[m0 * ys + col] = __float2bfloat16_rn(silu_ref(Act<__nv_bfloat16>::round(v4[0])) *
-                                                           Act<__nv_bfloat16>::round(v4[2]));
-                if (m1 < M)
-                    y[m1 * ys + col] = __float2bfloat16_rn(silu_ref(Act<__nv_bfloat16>::round(v4[1])) *
-                                                           Act<__nv_bfloat16>::round(v4[3]));
-            } else {
-                const int64_t n_lo = (int64_t)rb * 16 + g, n_hi = n_lo + 8;
-                const int ms[4] = {m0, m1, m0, m1};
-                const int64_t ns[4] = {n_lo, n_lo, n_hi, n_hi};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    if (ms[i] < M) {
-                        const int64_t off = ms[i] * n + ns[i];
-                        float o = Act<__nv_bfloat16>::round(v4[i]);
-                        if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD) o = o + __bfloat162float(y[off]);  // y is the residual
-                        y[off] = __float2bfloat16_rn(o);
-                    }
-                }
-            }
+        // lane (g, t): rows g and g+8 of the block, activation rows 2t and 2t+1
+        float* a16 = accs + (rb - lo) * 128;
+        atomicAdd(a16 + g * 8 + 2 * t, acc[0]);
+        atomicAdd(a16 + g * 8 + 2 * t + 1, acc[1]);
+        atomicAdd(a16 + (g + 8) * 8 + 2 * t, acc[2]);
+        atomicAdd(a16 + (g + 8) * 8 + 2 * t + 1, acc[3]);
+    }
+    r.slot = slot;
+    r.phase = phase;
+    ok = live;
+    named_bar_sync(kBarGemv, kDsCT);
+    ds_mark(p, l, m0 + 1);
+    // epilogue over (row block, weight row, activation row)
+    const float* rmul = stsh->row_mul;
+    const int nloc = hi - lo;
+    if constexpr (EPI == AMCU_EPI_SILU_MUL) {
+        // rows 0-7 of a block are gate rows 8 rb .. 8 rb + 7, rows 8-15 the matching up rows
+        const int64_t ys = n / 2;
+        for (int e = threadIdx.x; e < nloc * 8 * M; e += kDsCT) {
+            const int m = e % M, rr = (e / M) % 8, rl = e / (M * 8);
+            const float* a16 = accs + rl * 128;
+            const float gt = Act<__nv_bfloat16>::round(a16[rr * 8 + m] * rmul[m]);
+            const float up = Act<__nv_bfloat16>::round(a16[(rr + 8) * 8 + m] * rmul[m]);
+            y[m * ys + (int64_t)(lo + rl) * 8 + rr] = __float2bfloat16_rn(silu_ref(gt) * up);
+        }
+    } else {
+        for (int e = threadIdx.x; e < nloc * 16 * M; e += kDsCT) {
+            const int m = e % M, rr = (e / M) % 16, rl = e / (M * 16);
+            const int64_t off = m * n + (int64_t)(lo + rl) * 16 + rr;
+            float o = Act<__nv_bfloat16>::round(accs[rl * 128 + rr * 8 + m] * rmul[m]);
+            if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD) o = o + __bfloat162float(y[off]);  // y is the residual
+            y[off] = __float2bfloat16_rn(o);
         }
     }
 }
@@ -239,7 +305,8 @@ __device__ __noinline__ void ds_gemv(const DsParams& p, DsRing& r, int64_t n, in
 // CTAs; each writes a (max, sum, unnormalised output) partial, and the last
 // CTA to finish a (b, kv head) merges its ns splits into p.attn.
 template <int GRP, int D>
-__device__ __noinline__ void ds_attention(const DsParams& p, const AmcuDecodeLayer& ly, uint8_t* smem, const DsSmem& L, bool& ok) {
+__device__ __noinline__ void ds_attention(const DsParams& p, const AmcuDecodeLayer& ly, uint8_t* smem, const DsSmem& L, bool& ok,
+                                         int l) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t qkv_n = (p.nq + 2 * p.nkv) * D;
     uint8_t* u = smem + L.un;
@@ -269,11 +336,13 @@ __device__ __noinline__ void ds_attention(const DsParams& p, const AmcuDecodeLay
             rope_append_kv<D, true>(row + p.nq * D + (int64_t)kvh * D, row + (p.nq + p.nkv) * D + (int64_t)kvh * D,
                               kbase + pos * D, vbase + pos * D, pos, p.cos_sin, p.theta, threadIdx.x, kDsCT);
         named_bar_sync(kBarAttn, kDsCT);  // q staged; the appended row is visible to this CTA
+        if (un == blockIdx.x) ds_mark(p, l, 20);
         DecodeWarpState<GRP, D> st;
         DecodeKeyLoop<GRP, D, kDsConsumers> loop(kbase, vbase, k_begin, k_end, warp, lane);
         loop.run(qs, st);
         decode_publish_warp<GRP, D>(st, warp, lane, sm_m, sm_l, sm_o);
         named_bar_sync(kBarAttn, kDsCT);
+        if (un == blockIdx.x) ds_mark(p, l, 21);
         float* w = p.attn_ws + (((int64_t)b * p.nkv + kvh) * p.ns + sp) * GRP * (D + 2);
         for (int e = threadIdx.x; e < GRP * D; e += kDsCT) {
             const int h = e / D, dd = e % D;
@@ -293,15 +362,20 @@ __device__ __noinline__ void ds_attention(const DsParams& p, const AmcuDecodeLay
             if (*last) *cnt = 0;  // reset for the next layer (every arrival is in)
         }
         named_bar_sync(kBarAttn, kDsCT);
+        if (un == blockIdx.x) ds_mark(p, l, 22);
         if (*last) {
             // merge the ns partials: every split's (max, sum) to shared memory
             // first (one round of loads), then each output element sums its ns
             // terms with independent loads
             __threadfence();
             const float* w0 = p.attn_ws + ((int64_t)b * p.nkv + kvh) * p.ns * GRP * (D + 2);
-            float* fm = &sm_o[0][0][0];         // [ns][GRP] weights exp2(m - M) (sm_o is free now)
-            float* fl = fm + kDsMaxSplits * GRP; // [GRP] total sums
-            for (int i = threadIdx.x; i < p.ns * GRP; i += kDsCT) fm[i] = __ldcg(w0 + i * (D + 2));
+            float* fm = &sm_o[0][0][0];           // [ns][GRP] maxima, then weights exp2(m - M) (sm_o is free now)
+            float* fs = fm + kDsMaxSplits * GRP;   // [ns][GRP] sums
+            float* fl = fs + kDsMaxSplits * GRP;   // [GRP] total sums
+            for (int i = threadIdx.x; i < p.ns * GRP; i += kDsCT) {
+                fm[i] = __ldcg(w0 + i * (D + 2));
+                fs[i] = __ldcg(w0 + i * (D + 2) + 1);
+            }
             named_bar_sync(kBarAttn, kDsCT);
             if (threadIdx.x < GRP) {
                 const int h = threadIdx.x;
@@ -311,7 +385,7 @@ __device__ __noinline__ void ds_attention(const DsParams& p, const AmcuDecodeLay
                 for (int s = 0; s < p.ns; ++s) {
                     const float m = fm[s * GRP + h];
                     const float f = m == -INFINITY ? 0.f : exp2f(m - M);  // -inf: an empty split
-                    Ls += __ldcg(w0 + (s * GRP + h) * (D + 2) + 1) * f;
+                    Ls += fs[s * GRP + h] * f;
                     fm[s * GRP + h] = f;
                 }
                 fl[h] = Ls;
@@ -326,6 +400,7 @@ __device__ __noinline__ void ds_attention(const DsParams& p, const AmcuDecodeLay
             }
         }
         named_bar_sync(kBarAttn, kDsCT);  // shared memory is reused by the next unit
+        if (un == blockIdx.x) ds_mark(p, l, 23);
     }
     (void)ok;
 }
@@ -336,7 +411,7 @@ __global__ void __maxnreg__(96) decode_stack_kernel(DsParams p) {
     __shared__ StageShared stsh;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t kmax = p.I > p.H ? p.I : p.H;
-    const DsSmem L = ds_smem<GRP, D>(kmax, p.stages);
+    const DsSmem L = ds_smem<GRP, D>(kmax, p.stages, p.rbmax);
     DsRing r{smem + L.ring, reinterpret_cast<uint64_t*>(smem + L.bars),
              reinterpret_cast<uint64_t*>(smem + L.bars) + p.stages, p.stages, 0, 0u};
     if (threadIdx.x == 0) {
@@ -351,7 +426,7 @@ __global__ void __maxnreg__(96) decode_stack_kernel(DsParams p) {
 
     if (warp == kDsConsumers) {
         // ---- producer: the CTA's share of every layer's weights, in consumption order
-        if (lane == 0) {
+        if (lane == 0 && !(p.dbg_skip & 4)) {
             int slot = 0;
             uint32_t phase = 0;
             int64_t i = 0;
@@ -392,18 +467,31 @@ __global__ void __maxnreg__(96) decode_stack_kernel(DsParams p) {
     bool ok = true;
     for (int l = 0; l < p.nlayers; ++l) {
         const AmcuDecodeLayer& ly = p.layers[l];
+        ds_mark(p, l, 0);
         if (l > 0) ds_grid_barrier(p, ok);  // the previous layer's residual stream is complete
+        ds_mark(p, l, 1);
         ds_gemv<AMCU_EPI_STORE>(p, r, qkv_n, p.H, p.x, static_cast<const __nv_bfloat16*>(ly.attn_norm), p.qkv, smem, L,
-                                &stsh, ok);
+                                &stsh, ok, l, 2);
+        ds_mark(p, l, 4);
         ds_grid_barrier(p, ok);
-        if (!(p.dbg_skip & 1)) ds_attention<GRP, D>(p, ly, smem, L, ok);
+        ds_mark(p, l, 5);
+        if (!(p.dbg_skip & 1)) ds_attention<GRP, D>(p, ly, smem, L, ok, l);
+        ds_mark(p, l, 6);
         ds_grid_barrier(p, ok);
-        ds_gemv<AMCU_EPI_RESIDUAL_ADD>(p, r, p.H, p.nq * D, p.attn, nullptr, p.x, smem, L, &stsh, ok);
+        ds_mark(p, l, 7);
+        ds_prefetch_l2(ly.mlp_norm, p.H * 2);
+        ds_gemv<AMCU_EPI_RESIDUAL_ADD>(p, r, p.H, p.nq * D, p.attn, nullptr, p.x, smem, L, &stsh, ok, l, 8);
+        ds_mark(p, l, 10);
         ds_grid_barrier(p, ok);
+        ds_mark(p, l, 11);
         ds_gemv<AMCU_EPI_SILU_MUL>(p, r, 2 * p.I, p.H, p.x, static_cast<const __nv_bfloat16*>(ly.mlp_norm), p.act,
-                                   smem, L, &stsh, ok);
+                                   smem, L, &stsh, ok, l, 12);
+        ds_mark(p, l, 14);
         ds_grid_barrier(p, ok);
-        ds_gemv<AMCU_EPI_RESIDUAL_ADD>(p, r, p.H, p.I, p.act, nullptr, p.x, smem, L, &stsh, ok);
+        ds_mark(p, l, 15);
+        if (l + 1 < p.nlayers) ds_prefetch_l2(p.layers[l + 1].attn_norm, p.H * 2);
+        ds_gemv<AMCU_EPI_RESIDUAL_ADD>(p, r, p.H, p.I, p.act, nullptr, p.x, smem, L, &stsh, ok, l, 16);
+        ds_mark(p, l, 18);
     }
     pdl_trigger();
 }
@@ -412,6 +500,12 @@ template <int GRP, int D>
 static am_status_code launch_stack(DsParams p, cudaStream_t s) {
     auto kern = decode_stack_kernel<GRP, D>;
     const int64_t kmax = p.I > p.H ? p.I : p.H;
+    {
+        int64_t nmax = 2 * p.I > (p.nq + 2 * p.nkv) * D ? 2 * p.I : (p.nq + 2 * p.nkv) * D;
+        if (p.H > nmax) nmax = p.H;
+        const int ctas = num_sms();
+        p.rbmax = (int)((nmax / 16 + ctas - 1) / ctas);
+    }
     int dev = 0, smem_max = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
@@ -419,7 +513,7 @@ static am_status_code launch_stack(DsParams p, cudaStream_t s) {
     // as many ring stages as still let one CTA reside on every SM
     int stages = 12, bytes = 0;
     for (; stages >= 3; --stages) {
-        bytes = ds_smem<GRP, D>(kmax, stages).total;
+        bytes = ds_smem<GRP, D>(kmax, stages, p.rbmax).total;
         if (bytes > smem_max) continue;
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
         int per_sm = 0;
@@ -434,7 +528,7 @@ static am_status_code launch_stack(DsParams p, cudaStream_t s) {
         return set_error(AM_STATUS_INVALID_ARGUMENT,
                          "amcu_decode_stack: no CTA fits an SM (registers %d, max threads %d, static smem %zu, "
                          "dynamic smem %d)",
-                         fa.numRegs, fa.maxThreadsPerBlock, fa.sharedSizeBytes, ds_smem<GRP, D>(kmax, 3).total);
+                         fa.numRegs, fa.maxThreadsPerBlock, fa.sharedSizeBytes, ds_smem<GRP, D>(kmax, 3, p.rbmax).total);
     }
     p.stages = stages;
     cudaLaunchConfig_t cfg = {};
@@ -452,6 +546,20 @@ static am_status_code launch_stack(DsParams p, cudaStream_t s) {
         cudaGetLastError();
         return set_error(AM_STATUS_INTERNAL, "amcu_decode_stack launch: %s", cudaGetErrorString(e));
     }
+    if (p.trace) {
+        // diagnostics: append the stamps of this (eager, synchronised) step to the trace file
+        const size_t n = (size_t)num_sms() * p.nlayers * kDsMarks;
+        std::vector<unsigned long long> h(n);
+        if (cudaStreamSynchronize(s) == cudaSuccess &&
+            cudaMemcpy(h.data(), p.trace, n * 8, cudaMemcpyDeviceToHost) == cudaSuccess) {
+            if (FILE* f = std::fopen(std::getenv("AMCU_DS_TRACE"), "ab")) {
+                const int hdr[3] = {num_sms(), p.nlayers, kDsMarks};
+                std::fwrite(hdr, sizeof(hdr), 1, f);
+                std::fwrite(h.data(), 8, n, f);
+                std::fclose(f);
+            }
+        }
+    }
     return AM_STATUS_OK;
 }
 
@@ -466,7 +574,7 @@ size_t amcu_decode_stack_workspace_bytes(const AmcuDecodeStackArgs* a) {
     const int64_t grp = a->n_q_heads / (a->n_kv_heads > 0 ? a->n_kv_heads : 1);
     const size_t ws = (size_t)a->batch * a->n_kv_heads * kDsMaxSplits * grp * (a->head_dim + 2) * sizeof(float);
     const size_t cnt = (size_t)a->batch * a->n_kv_heads * sizeof(int32_t);
-    return 256 + (cnt + 255) / 256 * 256 + ws;
+    return kDsBarWords * 4 + (cnt + 255) / 256 * 256 + ws;
 }
 
 am_status_code amcu_decode_stack(const AmcuDecodeStackArgs* a, void* stream) {
@@ -503,8 +611,8 @@ am_status_code amcu_decode_stack(const AmcuDecodeStackArgs* a, void* stream) {
     p.scale_log2 = (float)(1.0 / sqrt((double)a->head_dim)) * kLog2e;
     uint8_t* w = static_cast<uint8_t*>(a->workspace);
     p.bar = reinterpret_cast<unsigned int*>(w);
-    p.attn_cnt = reinterpret_cast<int32_t*>(w + 256);
-    p.attn_ws = reinterpret_cast<float*>(w + 256 + ((size_t)a->batch * a->n_kv_heads * 4 + 255) / 256 * 256);
+    p.attn_cnt = reinterpret_cast<int32_t*>(w + kDsBarWords * 4);
+    p.attn_ws = reinterpret_cast<float*>(w + kDsBarWords * 4 + ((size_t)a->batch * a->n_kv_heads * 4 + 255) / 256 * 256);
     // splits: about one (sequence, kv head, split) unit per SM
     int ns = (int)(num_sms() / (a->batch * a->n_kv_heads));
     p.ns = ns < 1 ? 1 : (ns > kDsMaxSplits ? kDsMaxSplits : ns);
@@ -515,6 +623,24 @@ am_status_code amcu_decode_stack(const AmcuDecodeStackArgs* a, void* stream) {
         return v ? std::atoi(v) : 0;
     }();
     p.dbg_skip = dbg;
+    p.trace = nullptr;
+    if (std::getenv("AMCU_DS_TRACE")) {
+        // diagnostics only (eager sessions): one stamp buffer, grown on demand
+        static unsigned long long* buf = nullptr;
+        static size_t cap = 0;
+        const size_t n = (size_t)num_sms() * a->n_layers * kDsMarks;
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(as_stream(stream), &cs);
+        if (cs == cudaStreamCaptureStatusNone) {
+            if (n > cap) {
+                if (buf) cudaFree(buf);
+                buf = nullptr;
+                cap = 0;
+                if (cudaMalloc(&buf, n * 8) == cudaSuccess) cap = n;
+            }
+            p.trace = buf;
+        }
+    }
     const int grp = (int)(a->n_q_heads / a->n_kv_heads);
     const cudaStream_t s = as_stream(stream);
     if (a->head_dim == 128 && grp == 4) return launch_stack<4, 128>(p, s);

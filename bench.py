@@ -93,7 +93,7 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.rows)}
 
 
-def gemv_roofline(hbm_peak: float) -> dict:
+def gemv_roofline(hbm_peak: float, ncopy: int | None = None, reps: int | None = None) -> dict:
     """Times the W4 GEMV of the 8B gate/up projection (N = 2 x 14336, K = 4096)
     alone, rotating over enough weight copies that every launch reads HBM."""
     import ctypes as C
@@ -107,7 +107,7 @@ def gemv_roofline(hbm_peak: float) -> dict:
     q, s = ops.synth_w4(SEED, 99, n, k, 0.004)
     copies = []
     per = n * k // 2 + n * (k // 128) * 2
-    ncopy = max(2, int(512e6 // per) + 1)  # > 4 x L2
+    ncopy = ncopy or max(2, int(512e6 // per) + 1)  # > 4 x L2
     for _ in range(ncopy):
         copies.append(ops.prepack(L.WFMT_INT4, q, s, n, k))
     x = torch.randn(1, k, device="cuda").to(torch.bfloat16)
@@ -121,7 +121,7 @@ def gemv_roofline(hbm_peak: float) -> dict:
     for a in args[:4]:
         lib.amcu_gemv_w4g128(C.byref(a), stream)
     torch.cuda.synchronize()
-    reps = 20 * ncopy
+    reps = reps or 20 * ncopy
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(reps):
@@ -135,7 +135,61 @@ def gemv_roofline(hbm_peak: float) -> dict:
     torch.cuda.empty_cache()
     return {"kernel": "gemv_tc_kernel<INT4> (8B gate_up, n=28672 k=4096, m=1)", "bound": "hbm",
             "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(gbs / hbm_peak, 3),
-            "traffic": None, "alg_bytes_per_launch": alg, "us_per_launch": round(us, 2)}
+            # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel and shape,
+            # from the ncu capture summarised in profiles/gemv_w4_gate_up_8b.md
+            "traffic": GEMV_GATE_UP_TRAFFIC, "alg_bytes_per_launch": alg, "us_per_launch": round(us, 2)}
+
+
+GEMV_GATE_UP_TRAFFIC = 60635904
+
+
+def gemm_prefill_timing(tc_peak: float, reps: int = 20) -> dict:
+    """Times the tcgen05 prefill GEMM of the 8B gate/up projection, m = 512
+    prompt rows (n = 2 x 14336, k = 4096, INT4 g128, SiLU-Mul epilogue)."""
+    import ctypes as C
+
+    import torch
+
+    from aethermind_b200 import _lib as L
+    from aethermind_b200 import ops
+
+    m, inter, k = PROMPT, 14336, 4096
+    gq, gs = ops.synth_w4(SEED, 98, inter, k, 0.004)
+    uq, us_ = ops.synth_w4(SEED, 99, inter, k, 0.004)
+    pw = ops.prepack_gate_up(L.WFMT_INT4, gq, gs, uq, us_, inter, k)
+    x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    y = torch.empty(m, inter, device="cuda", dtype=torch.bfloat16)
+    a, _, _ = ops._linear_args(x, pw, L.EPI_SILU_MUL, None, y)
+    lib = L.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(3):
+        L.check(lib.amcu_gemm_w4g128_prefill(C.byref(a), stream), "amcu_gemm_w4g128_prefill")
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        lib.amcu_gemm_w4g128_prefill(C.byref(a), stream)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    tflops = 2.0 * m * 2 * inter * k / (us * 1e-6) / 1e12
+    return {"kernel": "gemm_tc_kernel<INT4, SILU_MUL> (8B gate_up, m=512 n=28672 k=4096)", "bound": "tensor",
+            "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s", "frac": round(tflops / tc_peak, 3),
+            "us_per_launch": round(us, 2)}
+
+
+def op_bench(args) -> None:
+    """Single-kernel timing for the profiles (one GPU): --op gemv_gate_up | gemm_gate_up."""
+    import torch
+    torch.cuda.set_device(0)
+    hbm_peak, tc_peak, _ = _peaks()
+    if args.op == "gemv_gate_up":
+        r = gemv_roofline(hbm_peak, ncopy=args.copies, reps=args.reps)
+    elif args.op == "gemm_gate_up":
+        r = gemm_prefill_timing(tc_peak, reps=args.reps or 20)
+    else:
+        raise SystemExit(f"unknown --op {args.op}")
+    print(json.dumps({"op": args.op, **r}), flush=True)
 
 
 def decode_bytes_per_token(cfg, ctx: float) -> float:
@@ -199,7 +253,13 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="debug: fewer layers (invalidates the number)")
+    ap.add_argument("--op", default=None, help="time one kernel instead: gemv_gate_up | gemm_gate_up")
+    ap.add_argument("--copies", type=int, default=None, help="--op gemv_gate_up: weight copies rotated")
+    ap.add_argument("--reps", type=int, default=None, help="--op: timed launches")
     args = ap.parse_args()
+    if args.op:
+        op_bench(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
@@ -301,6 +361,8 @@ def main() -> None:
         torch.cuda.empty_cache()
         line["roofline"] = gemv_roofline(hbm_peak)
         line["roofline"]["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+        line["prefill_roofline"] = gemm_prefill_timing(tc_peak)
+        line["prefill_roofline"]["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops, burst)"
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         ccfg = dataclasses.replace(cfg, max_seq=64)
         cb = cpu_oracle_decode(cpu_oracle_model(ccfg), ccfg, 8, 2)

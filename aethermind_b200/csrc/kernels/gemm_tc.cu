@@ -24,6 +24,10 @@
 // code), so a fault of the pipeline cannot hang the GPU.
 #include <cuda.h>
 
+#include <cstdio>
+#include <cstdlib>
+#include <vector>
+
 #include "../amcu_internal.h"
 #include "common.cuh"
 #include "gemm_tc.cuh"
@@ -48,6 +52,29 @@ struct GemmTcKParams {
     int64_t m, n, k;
     int64_t y_stride;
     int32_t* err;
+    unsigned long long* trace;  // diagnostics (AMCU_GEMM_TRACE): per CTA [16] cycle counters, or null
+    int dbg;  // diagnostics (AMCU_GEMM_DBG, wrong results): bit 0 skips the dequant math, bit 1 the promotion, bit 2 the stores, bit 3 the epilogue's staging,
+              // bit 4 the activation loads, bit 5 the record loads (swapped kernel)
+};
+
+// Diagnostics: a globaltimer stamp into slot `slot` of this CTA's counters.
+__device__ __forceinline__ void tc_stamp(const GemmTcKParams& p, int slot) {
+    if (!p.trace) return;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    p.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 16 + slot] = t;
+}
+
+// Diagnostics: cycles spent in a wait or a phase, summed per CTA and role.
+struct TcClock {
+    long long t0 = 0;
+    __device__ __forceinline__ void start(const GemmTcKParams& p) {
+        if (p.trace) t0 = clock64();
+    }
+    __device__ __forceinline__ void stop(const GemmTcKParams& p, int slot) {
+        if (p.trace) atomicAdd(p.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 16 + slot,
+                               (unsigned long long)(clock64() - t0));
+    }
 };
 
 // ---- tcgen05 / TMA helpers (inline PTX) ----
@@ -373,6 +400,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     tc_fence_after();
     const uint32_t taddr = *tmem_slot;
     bool ok = true;
+    TcClock whole;
+    if (threadIdx.x == 0) whole.start(p);
 
     if (warp == kTcDequantWarps) {
         // ---- TMA producer: x tiles (the activations come from the previous kernel)
@@ -412,8 +441,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             for (int kb = 0; kb < KB; ++kb) {
                 const int s = kb % kTcStages;
                 const uint32_t par = (kb / kTcStages) & 1;
-                if (ok && (!mbar_wait(&full_a[s], par) || !mbar_wait(&full_b[s], par))) ok = false;
+                TcClock ck;
+                ck.start(p);
+                if (ok && !mbar_wait(&full_a[s], par)) ok = false;
+                ck.stop(p, 0);  // 0: MMA waits for the TMA stage
+                ck.start(p);
+                if (ok && !mbar_wait(&full_b[s], par)) ok = false;
+                ck.stop(p, 1);  // 1: MMA waits for the dequantized weights
+                ck.start(p);
                 if (W4 && ok && kb >= 2 && !mbar_wait(&tempty[kb & 1], ((kb >> 1) & 1) ^ 1)) ok = false;
+                ck.stop(p, 2);  // 2: MMA waits for a free accumulator buffer
                 if (!ok) {
                     record_device_error(p.err, kErrGemmTcWait);
                     break;
@@ -438,6 +475,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         const int quarter = warp & 3, half = warp >> 2;
         const int row = m0 + quarter * 32 + lane;  // TMEM lane of this thread = tile row
         auto produce = [&](int kb) {
+            TcClock ck;
+            if (warp == 0 && lane == 0) ck.start(p);
             const int s = kb % kTcStages;
             if constexpr (W4) {
                 // the TMA warp staged this stage's records after the stage was released
@@ -450,13 +489,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
             }
             if (!ok) return;
-            if constexpr (W4)
-                dequant_rows_w4_exact(p, rb, Ws + s * kTcWStage + warp * kW4PairBytes, warp, lane, Bs + s * kTcTileBytes,
-                                      scl + (kb % kScl) * kTcBN);
-            else dequant_rows<FMT>(p, rb, kb, warp, lane, Bs + s * kTcTileBytes);
+            if (!(p.dbg & 1)) {
+                if constexpr (W4)
+                    dequant_rows_w4_exact(p, rb, Ws + s * kTcWStage + warp * kW4PairBytes, warp, lane,
+                                          Bs + s * kTcTileBytes, scl + (kb % kScl) * kTcBN);
+                else dequant_rows<FMT>(p, rb, kb, warp, lane, Bs + s * kTcTileBytes);
+            }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
             __syncwarp();
             if (lane == 0) mbar_arrive(&full_b[s]);
+            if (warp == 0 && lane == 0) ck.stop(p, 3);  // 3: dequant warp 0 producing a stage
         };
         float acc[64];
 #pragma unroll
@@ -464,14 +506,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         if constexpr (W4) {
             for (int kb = 0; kb < kTcStages && kb < KB; ++kb) produce(kb);
             for (int kb = 0; kb < KB; ++kb) {
+                TcClock ck;
+                if (warp == 0 && lane == 0) ck.start(p);
                 if (ok && !mbar_wait(&tfull[kb & 1], (kb >> 1) & 1)) {
                     ok = false;
                     if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
                 }
+                if (warp == 0 && lane == 0) ck.stop(p, 4);  // 4: dequant warp 0 waits for the MMAs
+                if (warp == 0 && lane == 0) ck.start(p);
                 tc_fence_after();
                 const float* sc = scl + (kb % kScl) * kTcBN + half * 64;
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
+                    if (p.dbg & 2) break;
                     uint32_t r[32];
                     tc_ld_32x32b_x32(taddr + (uint32_t)((kb & 1) * kTcBN) + ((uint32_t)(quarter * 32) << 16) +
                                              (uint32_t)(half * 64 + c * 32),
@@ -488,6 +535,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[kb & 1]);
+                if (warp == 0 && lane == 0) ck.stop(p, 5);  // 5: dequant warp 0 promoting
                 if (kb + kTcStages < KB) produce(kb + kTcStages);
             }
         } else {
@@ -506,8 +554,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             }
         }
         // ---- epilogue: this thread's row, columns half * 64 .. + 63
+        TcClock cke;
+        if (warp == 0 && lane == 0) cke.start(p);
         pdl_wait();
-        if (row < p.m && ok) {
+        if (row < p.m && ok && !(p.dbg & 4)) {
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 float v[32];
@@ -517,12 +567,381 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             }
         }
         pdl_trigger();
+        if (warp == 0 && lane == 0) cke.stop(p, 7);  // 7: epilogue
     }
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) whole.stop(p, 6);  // 6: CTA main body
     if (warp == kTcDequantWarps + 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(kTmemCols) : "memory");
+    }
+}
+
+
+// ---------------------------------------------------------------------------
+// INT4 with the operands swapped: out^T = W x^T. The dequantized weights are
+// the MMA's A operand and go from registers straight into tensor memory
+// (tcgen05.st), the activations are B (TMA, 128-byte swizzle). Shared memory
+// then carries only the activation tiles (written by TMA, read once by the
+// tensor cores) and the pair records, about half the bytes per FLOP of the
+// kernel above, whose bf16 weight tiles are written and read through shared
+// memory. A CTA computes 128 weight rows x 128 tokens.
+//
+// Tensor memory (512 columns): D0 [0, 128) and D1 [128, 256) hold the
+// partial sums of one K block (one scale group) each, A stage s at
+// [256 + 64 s, +64) holds 128 weight rows x 128 K as bf16 pairs.
+//
+// Warps 0-7: warp w dequantizes weight rows 32 (w % 4) .. +31 (its TMEM lane
+// quarter), K half w / 4 of every block, then folds the partial sums of the
+// same rows, token half w / 4, into registers with each row's group scale,
+// and finally stores those outputs. Warp 8: TMA of the activation tile and
+// the 8 pair records per stage. Warp 9: TMEM owner and MMA issuer.
+constexpr int kSwStages = 4;   // shared-memory activation stages
+constexpr int kSwWStages = 8;  // shared-memory pair-record stages (their own producer warp runs ahead)
+constexpr int kSwAStages = 4;  // TMEM weight stages (64 columns each, after the 256 accumulator columns)
+constexpr int kSwXBytes = kTcBN * kTcBK * 2;  // activation tile: 128 tokens x 128 K
+constexpr int kSwDqWarps = 16;                // dequant / promotion / epilogue warps
+constexpr int kSwThreads = (kSwDqWarps + 3) * 32;  // + activation TMA warp, MMA warp, record warp
+constexpr int kSwSmemBytes = 1024 + kSwStages * kSwXBytes + kSwWStages * kTcWStage + (kSwAStages + 2) * kTcBM * 4 + 512;
+
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+            " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+            "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc)
+            : "memory");
+}
+__device__ __forceinline__ void tc_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+            "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+            "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+            "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+            "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+            "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+            : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_st_32x32b_x16_nowait(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+            "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+            "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+            : "memory");
+}
+__device__ __forceinline__ void tc_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+            "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+            "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+            : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kSwThreads, 1) gemm_w4_swap_kernel(const __grid_constant__ CUtensorMap tmx,
+                                                                      GemmTcKParams p) {
+    constexpr int S = kSwStages, SA = kSwAStages, SW = kSwWStages;
+    static_assert(S == SA, "one release per K block frees the activation stage and the TMEM weight stage");
+    constexpr int kScl = SA + 2;  // scale ring: entry kb % kScl is rewritten only after promotion(kb)
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* Xs = smem;                                                  // [S][32 KB] activations
+    uint8_t* Ws = smem + S * kSwXBytes;                                  // [SW][8 pair records]
+    float* scl = reinterpret_cast<float*>(Ws + SW * kTcWStage);          // [kScl][128] row scales
+    uint64_t* full = reinterpret_cast<uint64_t*>(scl + kScl * kTcBM);    // [S] activation stage landed (TMA)
+    uint64_t* fulla = full + S;                                          // [SA] weights of TMEM stage in place
+    uint64_t* empty = fulla + SA;                                        // [S] MMAs of the activation stage done
+    uint64_t* fullw = empty + S;                                         // [SW] record stage landed
+    uint64_t* wempty = fullw + SW;                                       // [SW] record stage read by the dequant warps
+    uint64_t* tfull = wempty + SW;                                       // [2] partial sums ready
+    uint64_t* tempty = tfull + 2;                                        // [2] partial sums folded
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    int* dq_fail = reinterpret_cast<int*>(tmem_slot + 1);  // a dequant-side wait ran out
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) tc_stamp(p, 9);  // CTA start
+    const int m0 = blockIdx.x * kTcBN;                 // first token
+    const int64_t n0 = (int64_t)blockIdx.y * kTcBM;    // first weight row
+    const int KB = (int)(p.k / kTcBK);
+
+    if (warp == kSwDqWarps + 1) {
+        if (lane == 0) {
+            for (int s = 0; s < S; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            for (int s = 0; s < SA; ++s) mbar_init(&fulla[s], kSwDqWarps);
+            *dq_fail = 0;
+            for (int s = 0; s < SW; ++s) {
+                mbar_init(&fullw[s], 1);
+                mbar_init(&wempty[s], kSwDqWarps);
+            }
+            for (int b = 0; b < 2; ++b) {
+                mbar_init(&tfull[b], 1);
+                mbar_init(&tempty[b], kSwDqWarps);
+            }
+            fence_mbar_init();
+        }
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t taddr = *tmem_slot;
+    bool ok = true;
+    TcClock whole;
+    if (threadIdx.x == 0) whole.start(p);
+
+    if (warp == kSwDqWarps) {
+        // ---- TMA producer of the activation tiles (they come from the previous kernel)
+        pdl_wait();
+        if (lane == 0) {
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % S;
+                if (kb >= S && ok && !mbar_wait(&empty[s], ((kb / S) & 1) ^ 1)) {
+                    ok = false;
+                    record_device_error(p.err, kErrGemmTcWait);
+                }
+                if (!ok) break;
+                if (p.dbg & 16) {  // diagnostics: no activation loads
+                    mbar_arrive(&full[s]);
+                    continue;
+                }
+                mbar_expect_tx(&full[s], (uint32_t)kSwXBytes);
+                uint8_t* dst = Xs + s * kSwXBytes;
+                tma_load_2d(dst, &tmx, kb * kTcBK, m0, &full[s]);
+                tma_load_2d(dst + kSwXBytes / 2, &tmx, kb * kTcBK + 64, m0, &full[s]);
+            }
+        }
+    } else if (warp == kSwDqWarps + 2) {
+        // ---- producer of the pair records (weights: no dependence on the previous kernel)
+        if (lane == 0) {
+            const int64_t rem = (p.n - n0) / 16;
+            const int nrec = rem < kTcBM / 16 ? (int)rem : kTcBM / 16;
+            const int64_t G = p.k / 128;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % SW;
+                if (kb >= SW && ok && !mbar_wait(&wempty[s], ((kb / SW) & 1) ^ 1)) {
+                    ok = false;
+                    record_device_error(p.err, kErrGemmTcWait);
+                }
+                if (!ok) break;
+                if (p.dbg & 32) {  // diagnostics: no record loads
+                    mbar_arrive(&fullw[s]);
+                    continue;
+                }
+                mbar_expect_tx(&fullw[s], (uint32_t)(nrec * kW4PairBytes));
+                for (int w = 0; w < nrec; ++w)
+                    bulk_g2s(Ws + s * kTcWStage + w * kW4PairBytes, p.w + ((size_t)(n0 / 16 + w) * G + kb) * kW4PairBytes,
+                             kW4PairBytes, &fullw[s]);
+            }
+        }
+    } else if (warp == kSwDqWarps + 1) {
+        // ---- MMA issuer: D[kb & 1] = W_tile(kb) x X_tile(kb)^T over the block's 8 K steps
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc_idesc_bf16(kTcBM, kTcBN);
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % S;
+                const uint32_t par = (kb / S) & 1;
+                TcClock ck;
+                ck.start(p);
+                if (ok && !mbar_wait(&full[s], par)) ok = false;
+                ck.stop(p, 0);
+                ck.start(p);
+                if (ok && !mbar_wait(&fulla[kb % SA], (kb / SA) & 1)) ok = false;
+                ck.stop(p, 1);
+                ck.start(p);
+                if (ok && kb >= 2 && !mbar_wait(&tempty[kb & 1], ((kb >> 1) & 1) ^ 1)) ok = false;
+                ck.stop(p, 2);
+                if (kb == 0) tc_stamp(p, 8);
+                if (!ok) {
+                    record_device_error(p.err, kErrGemmTcWait);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t b0 = smem_u32(Xs + s * kSwXBytes);
+                const uint32_t d = taddr + (uint32_t)((kb & 1) * kTcBN);
+                const uint32_t a = taddr + 256u + (uint32_t)(64 * (kb % SA));
+#pragma unroll
+                for (int j = 0; j < kTcBK / 16; ++j) {
+                    // K step j: 16 bf16 = 8 TMEM columns of A; 32 bytes per step in the swizzled B rows
+                    const uint32_t off = (uint32_t)((j >> 2) * (kSwXBytes / 2) + (j & 3) * 32);
+                    tc_mma_ts(d, a + (uint32_t)(8 * j), tc_desc_sw128(b0 + off), idesc, j != 0);
+                }
+                if (kb == KB - 1) tc_stamp(p, 10);  // last MMAs issued
+                tc_commit(&empty[s]);        // activation stage and TMEM weight stage free
+                tc_commit(&tfull[kb & 1]);  // partial sums of this block ready
+            }
+        }
+    } else {
+        // ---- dequant / promotion / epilogue warps: warp w serves TMEM lane
+        // quarter q = w % 4 (weight rows 32 q .. +31, one per lane) and part
+        // pt = w / 4: K columns 32 pt .. +31 of every block when producing,
+        // tokens 32 pt .. +31 when promoting and storing
+        const int q = warp & 3, pt = warp >> 2;
+        const int r = q * 32 + lane;  // weight row in the tile = TMEM lane
+        const int blk = r >> 4, rr = r & 15, g = rr & 7, hi = rr >> 3;
+        const int64_t rb = n0 / 16 + blk;
+        const bool valid = rb * 16 < p.n;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        int pending = -1;  // stage whose TMEM store is issued but not yet published
+        // completes the TMEM store of the last produced stage and hands it to the MMA warp
+        auto publish = [&]() {
+            if (pending < 0) return;
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&fulla[pending % SA]);
+            pending = -1;
+        };
+        auto dq_wait = [&](uint64_t* b1, uint32_t par1, uint64_t* b2, uint32_t par2) {
+            if (ok && (!mbar_wait(b1, par1) || (b2 && !mbar_wait(b2, par2)))) {
+                ok = false;
+                if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
+            }
+        };
+        auto produce = [&](int kb) {
+            TcClock ck;
+            if (warp == 0 && lane == 0) ck.start(p);
+            const int sw = kb % SW, sa = kb % SA;
+            dq_wait(&fullw[sw], (kb / SW) & 1, kb >= SA ? &empty[sa] : nullptr, ((kb / SA) & 1) ^ 1);
+            if (!ok) return;
+            publish();
+            const uint8_t* rec = Ws + sw * kTcWStage + blk * kW4PairBytes;
+            uint32_t v[16];
+            if (valid && !(p.dbg & 1)) {
+                if (pt == 0)
+                    scl[(kb % kScl) * kTcBM + r] =
+                            __half2float(reinterpret_cast<const __half*>(rec + 1024)[2 * g + hi]);
+                // Rows g and g+8 of the 16-row block share the 64 bytes at 64 g of
+                // tile pt / 2 (K columns 64 (pt / 2) .. +63); word 4t + j covers
+                // columns 16t + 4j .. +3 as nibbles p0 p4 p2 p6 (row g) / p1 p5 p3 p7
+                // (row g+8). Part pt takes the 32 bytes of its 32 columns.
+                const uint4* src = reinterpret_cast<const uint4*>(rec + (pt >> 1) * 512 + g * 64 + (pt & 1) * 32);
+                const uint4 wa = src[0], wb = src[1];
+                const uint32_t w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                const __nv_bfloat162 bias = __floats2bfloat162_rn(136.f, 136.f);
+                const uint32_t sh = 4u * (uint32_t)hi;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t lo2, hi2;
+                    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(lo2) : "r"(w8[j] >> sh), "r"(0x000F000Fu), "r"(0x43084308u));
+                    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(hi2) : "r"(w8[j] >> (sh + 8)), "r"(0x000F000Fu), "r"(0x43084308u));
+                    __nv_bfloat162 b0 = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&lo2), bias);
+                    __nv_bfloat162 b1 = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&hi2), bias);
+                    v[2 * j] = *reinterpret_cast<uint32_t*>(&b0);
+                    v[2 * j + 1] = *reinterpret_cast<uint32_t*>(&b1);
+                }
+            } else {
+                if (pt == 0) scl[(kb % kScl) * kTcBM + r] = 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] = 0u;
+            }
+            tc_st_32x32b_x16_nowait(taddr + lane_base + 256u + (uint32_t)(64 * sa + 16 * pt), v);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&wempty[sw]);  // records read (the scale went to scl)
+            pending = kb;
+            if (warp == 0 && lane == 0) ck.stop(p, 3);
+        };
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+        for (int kb = 0; kb < SA && kb < KB; ++kb) produce(kb);
+        publish();
+        for (int kb = 0; kb < KB; ++kb) {
+            TcClock ck;
+            if (warp == 0 && lane == 0) ck.start(p);
+            dq_wait(&tfull[kb & 1], (kb >> 1) & 1, nullptr, 0);
+            if (warp == 0 && lane == 0) ck.stop(p, 4);
+            if (warp == 0 && lane == 0) ck.start(p);
+            tc_fence_after();
+            const float sc = scl[(kb % kScl) * kTcBM + r];
+            if (!(p.dbg & 2)) {
+                uint32_t t32[32];
+                tc_ld_32x32b_x32(taddr + lane_base + (uint32_t)((kb & 1) * kTcBN + 32 * pt), t32);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[i] = fmaf(sc, __uint_as_float(t32[i]), acc[i]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[kb & 1]);
+            if (warp == 0 && lane == 0) ck.stop(p, 5);
+            if (kb + SA < KB) produce(kb + SA);
+            if (kb + 1 + SA >= KB) publish();  // nothing produced after this one
+        }
+        publish();
+        if (warp == 0 && lane == 0) tc_stamp(p, 11);  // last promotion done
+        // ---- epilogue: the tile goes through shared memory (the first activation
+        // stage, idle now: every MMA has completed) as [128 tokens][128 or 64
+        // columns] bf16, then out with 16-byte row stores
+        TcClock cke;
+        if (warp == 0 && lane == 0) cke.start(p);
+        constexpr bool SILU = EPI == AMCU_EPI_SILU_MUL;
+        constexpr int OC = SILU ? kTcBM / 2 : kTcBM;  // output columns of the tile
+        __nv_bfloat16* T = reinterpret_cast<__nv_bfloat16*>(Xs);
+        const int tb = 32 * pt;  // this thread's first token in the tile
+        if (p.dbg & 8) {
+        } else if constexpr (SILU) {
+            // rows 0-7 of a 16-row block are gate rows, 8-15 the matching up
+            // rows: lanes g and g+8 swap one value per token pair, so each
+            // computes one of the two outputs
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+                const float send = hi ? acc[i] : acc[i + 1];
+                const float recv = __shfl_xor_sync(0xffffffffu, send, 8);
+                const float gt = hi ? recv : acc[i], up = hi ? acc[i + 1] : recv;
+                T[(tb + i + hi) * OC + blk * 8 + g] =
+                        __float2bfloat16_rn(silu_ref(Act<__nv_bfloat16>::round(gt)) * Act<__nv_bfloat16>::round(up));
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) T[(tb + i) * OC + r] = __float2bfloat16_rn(Act<__nv_bfloat16>::round(acc[i]));
+        }
+        named_bar_sync(1, kSwDqWarps * 32);
+        pdl_wait();
+        if (ok && !(p.dbg & 4)) {
+            const int64_t c0 = SILU ? n0 / 2 : n0;          // first output column of the tile
+            const int64_t cend = SILU ? p.n / 2 : p.n;
+            constexpr int CH = OC / 8;                      // 16-byte chunks per token row
+            for (int e = threadIdx.x; e < kTcBN * CH; e += kSwDqWarps * 32) {
+                const int tr = e / CH, ch = e % CH;
+                const int64_t col = c0 + ch * 8;
+                if (m0 + tr >= p.m || col >= cend) continue;
+                uint4 v = *reinterpret_cast<const uint4*>(T + tr * OC + ch * 8);
+                const int64_t off = (int64_t)(m0 + tr) * p.y_stride + col;
+                if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD) {
+                    const uint4 rv = *reinterpret_cast<const uint4*>(p.residual + off);
+                    uint32_t a4[4] = {v.x, v.y, v.z, v.w};
+                    const uint32_t r4[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float lo = __uint_as_float(a4[j] << 16) + __uint_as_float(r4[j] << 16);
+                        const float hi2 = __uint_as_float(a4[j] & 0xffff0000u) + __uint_as_float(r4[j] & 0xffff0000u);
+                        __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi2);
+                        a4[j] = *reinterpret_cast<uint32_t*>(&h2);
+                    }
+                    v = make_uint4(a4[0], a4[1], a4[2], a4[3]);
+                }
+                *reinterpret_cast<uint4*>(p.y + off) = v;
+            }
+        }
+        if (warp == 0 && lane == 0) cke.stop(p, 7);
+        if (warp == 0 && lane == 0) tc_stamp(p, 12);  // epilogue done
+        pdl_trigger();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0) whole.stop(p, 6);
+    if (warp == kSwDqWarps + 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(512) : "memory");
     }
 }
 
@@ -556,6 +975,41 @@ bool gemm_tc_supported(const GemmTcParams& p, int fmt) {
 }
 size_t gemm_tc_workspace_bytes(const GemmTcParams&, int) { return 0; }
 
+static int gemm_dbg() {
+    static const int v = [] {
+        const char* e = std::getenv("AMCU_GEMM_DBG");
+        return e ? std::atoi(e) : 0;
+    }();
+    return v;
+}
+
+// Diagnostics (AMCU_GEMM_TRACE=file, eager runs only): per-CTA cycle counters
+// of one launch, appended to the file when the launch has finished.
+struct TcTrace {
+    unsigned long long* buf = nullptr;
+    size_t n = 0;
+    dim3 grid;
+    cudaStream_t s;
+    TcTrace(dim3 g, cudaStream_t st) : grid(g), s(st) {
+        static const char* path = std::getenv("AMCU_GEMM_TRACE");
+        if (!path) return;
+        n = (size_t)g.x * g.y * 16;
+        if (cudaMalloc(&buf, n * 8) != cudaSuccess || cudaMemsetAsync(buf, 0, n * 8, s) != cudaSuccess) buf = nullptr;
+    }
+    ~TcTrace() {
+        if (!buf) return;
+        std::vector<unsigned long long> h(n);
+        if (cudaStreamSynchronize(s) == cudaSuccess && cudaMemcpy(h.data(), buf, n * 8, cudaMemcpyDeviceToHost) == cudaSuccess)
+            if (FILE* f = std::fopen(std::getenv("AMCU_GEMM_TRACE"), "ab")) {
+                const int hdr[2] = {(int)grid.x, (int)grid.y};
+                std::fwrite(hdr, sizeof(hdr), 1, f);
+                std::fwrite(h.data(), 8, n, f);
+                std::fclose(f);
+            }
+        cudaFree(buf);
+    }
+};
+
 template <int FMT, int EPI>
 static am_status_code launch_tc(const GemmTcParams& g, const CUtensorMap& map, cudaStream_t s) {
     auto kern = gemm_tc_kernel<FMT, EPI>;
@@ -574,8 +1028,36 @@ static am_status_code launch_tc(const GemmTcParams& g, const CUtensorMap& map, c
     p.k = g.k;
     p.y_stride = g.y_stride;
     p.err = device_error_word();
+    p.dbg = gemm_dbg();
     const dim3 grid((unsigned)((g.m + kTcBM - 1) / kTcBM), (unsigned)((g.n + kTcBN - 1) / kTcBN));
+    TcTrace tr(grid, s);
+    p.trace = tr.buf;
     launch_pdl(kern, grid, dim3(kTcThreads), (size_t)kTcSmemBytes, s, map, p);
+    return AM_STATUS_OK;
+}
+
+template <int EPI>
+static am_status_code launch_swap(const GemmTcParams& g, const CUtensorMap& map, cudaStream_t s) {
+    auto kern = gemm_w4_swap_kernel<EPI>;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSwSmemBytes);
+        attr = true;
+    }
+    GemmTcKParams p{};
+    p.w = static_cast<const uint8_t*>(g.w);
+    p.y = static_cast<__nv_bfloat16*>(g.y);
+    p.residual = static_cast<const __nv_bfloat16*>(g.residual);
+    p.m = g.m;
+    p.n = g.n;
+    p.k = g.k;
+    p.y_stride = g.y_stride;
+    p.err = device_error_word();
+    p.dbg = gemm_dbg();
+    const dim3 grid((unsigned)((g.m + kTcBN - 1) / kTcBN), (unsigned)((g.n + kTcBM - 1) / kTcBM));
+    TcTrace tr(grid, s);
+    p.trace = tr.buf;
+    launch_pdl(kern, grid, dim3(kSwThreads), (size_t)kSwSmemBytes, s, map, p);
     return AM_STATUS_OK;
 }
 
@@ -593,6 +1075,15 @@ am_status_code launch_gemm_tc(const GemmTcParams& g, int fmt, int epi, cudaStrea
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(AM_STATUS_INTERNAL, "cuTensorMapEncodeTiled failed (%d)", (int)r);
 #define AMCU_TC(F, E) return launch_tc<F, E>(g, map, s)
+    static const bool swap = [] {
+        const char* v = std::getenv("AMCU_GEMM_SWAP");
+        return !(v && v[0] == '0');
+    }();
+    if (fmt == AMCU_WFMT_INT4 && swap) {
+        if (epi == AMCU_EPI_STORE) return launch_swap<AMCU_EPI_STORE>(g, map, s);
+        if (epi == AMCU_EPI_RESIDUAL_ADD) return launch_swap<AMCU_EPI_RESIDUAL_ADD>(g, map, s);
+        return launch_swap<AMCU_EPI_SILU_MUL>(g, map, s);
+    }
     if (fmt == AMCU_WFMT_INT4) {
         if (epi == AMCU_EPI_STORE) AMCU_TC(AMCU_WFMT_INT4, AMCU_EPI_STORE);
         if (epi == AMCU_EPI_RESIDUAL_ADD) AMCU_TC(AMCU_WFMT_INT4, AMCU_EPI_RESIDUAL_ADD);

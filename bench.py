@@ -173,7 +173,7 @@ def gemm_prefill_timing(tc_peak: float, reps: int = 20) -> dict:
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / reps
     tflops = 2.0 * m * 2 * inter * k / (us * 1e-6) / 1e12
-    return {"kernel": "gemm_tc_kernel<INT4, SILU_MUL> (8B gate_up, m=512 n=28672 k=4096)", "bound": "tensor",
+    return {"kernel": "gemm_w4_swap_kernel<SILU_MUL> (8B gate_up, m=512 n=28672 k=4096)", "bound": "tensor",
             "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s", "frac": round(tflops / tc_peak, 3),
             "us_per_launch": round(us, 2)}
 

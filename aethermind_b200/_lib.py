@@ -144,6 +144,8 @@ _SIGS = {
     "am_runtime_create": (P, [C.POINTER(AmConfig)]),
     "am_runtime_destroy": (None, [P]),
     "am_nccl_get_unique_id": (C.c_int, [P]),
+    "am_runtime_peer_handle": (C.c_int, [P, P]),
+    "am_runtime_open_peers": (C.c_int, [P, P]),
     "am_last_error": (C.c_char_p, []),
     "am_model_load": (P, [P, C.c_char_p, C.POINTER(P)]),
     "am_model_create": (P, [P, C.POINTER(AmModelConfig), C.POINTER(P)]),

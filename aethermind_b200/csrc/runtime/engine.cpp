@@ -2,6 +2,11 @@
 // communicator of the CUDA backend.
 #include "runtime/engine.h"
 
+#include <cuda_runtime.h>
+
+#include "amcu_internal.h"
+#include "kernels/allreduce.cuh"
+
 #include <dlfcn.h>
 
 #include <cstdlib>
@@ -309,6 +314,68 @@ Status Communicator::Init(int rank, int world, const void* uid) {
 
 Communicator::~Communicator() {
     if (comm_ && nccl().CommDestroy) nccl().CommDestroy(comm_);
+    for (int r = 0; r < world_ && r < 8; ++r)
+        if (peers_[r] && peers_[r] != area_) cudaIpcCloseMemHandle(peers_[r]);
+    if (area_) cudaFree(area_);
+}
+
+Status Communicator::PeerHandle(void* out64) {
+    if (world_ <= 1) return Status::InvalidArgument("peer exchange needs tp_size > 1");
+    if (world_ > amcu::kArMaxRanks) return Status::InvalidArgument("peer exchange supports at most 8 ranks");
+    if (!area_) {
+        const size_t bytes = amcu::ar_area_bytes();
+        if (cudaMalloc(&area_, bytes) != cudaSuccess) {
+            area_ = nullptr;
+            cudaGetLastError();
+            return Status::ResourceExhausted("peer exchange area");
+        }
+        if (cudaMemset(area_, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
+            return Status::Internal("peer exchange area: memset failed");
+    }
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, area_) != cudaSuccess) {
+        cudaGetLastError();
+        return Status::Unavailable("cudaIpcGetMemHandle failed");
+    }
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    std::memcpy(out64, &h, 64);
+    return Status::Ok();
+}
+
+Status Communicator::OpenPeers(const void* handles) {
+    if (!area_) return Status::FailedPrecondition("call am_runtime_peer_handle first");
+    if (peers_open_) return Status::Ok();
+    for (int r = 0; r < world_; ++r) {
+        if (r == rank_) {
+            peers_[r] = area_;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const char*>(handles) + 64 * r, 64);
+        if (cudaIpcOpenMemHandle(&peers_[r], h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            peers_[r] = nullptr;
+            cudaGetLastError();
+            return Status::Unavailable("cudaIpcOpenMemHandle failed for rank " + std::to_string(r));
+        }
+    }
+    peers_open_ = true;
+    return Status::Ok();
+}
+
+bool Communicator::OneShotReady(int64_t n) const { return peers_open_ && amcu::ar_oneshot_supported(n, world_); }
+
+Status Communicator::AllReduceAddBf16(const void* part, void* x, int64_t n, cudaStream_t s) {
+    amcu::ArParams p{};
+    p.part = part;
+    p.x = x;
+    p.n = n;
+    p.rank = rank_;
+    p.world = world_;
+    for (int r = 0; r < world_; ++r) p.area[r] = static_cast<uint8_t*>(peers_[r]);
+    p.err = amcu::device_error_word();
+    amcu::launch_ar_oneshot_add(p, s);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? Status::Ok() : Status::Internal(std::string("one-shot all-reduce: ") + cudaGetErrorString(e));
 }
 
 Status Communicator::AllReduceSumBf16(void* buf, size_t n, cudaStream_t s) {

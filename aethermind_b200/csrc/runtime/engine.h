@@ -194,9 +194,20 @@ public:
     int world() const { return world_; }
     bool active() const { return comm_ != nullptr; }
 
+    // One-shot all-reduce over peer memory (no NCCL): this rank's exchange
+    // area is exported as a CUDA IPC handle, the peers' areas are opened from
+    // theirs; then x += sum of the ranks' partials runs as one kernel.
+    Status PeerHandle(void* out64);
+    Status OpenPeers(const void* handles);  // world x 64 bytes, rank order
+    bool OneShotReady(int64_t n) const;
+    Status AllReduceAddBf16(const void* part, void* x, int64_t n, cudaStream_t s);
+
 private:
     void* comm_ = nullptr;
     int rank_ = 0, world_ = 1;
+    void* area_ = nullptr;          // this rank's exchange area
+    void* peers_[8] = {};           // every rank's area as mapped here
+    bool peers_open_ = false;
 };
 Status NcclGetUniqueId(void* out128);
 

@@ -293,6 +293,17 @@ Status AllReduceStep(void* ctx, cudaStream_t s) noexcept {
     auto* a = static_cast<AllReduceCtx*>(ctx);
     return a->comm->AllReduceSumBf16(a->buf, a->count, s);
 }
+// x += all-reduce(partial) in one kernel over peer memory
+struct PeerAllReduceCtx {
+    Communicator* comm;
+    const void* part;
+    void* x;
+    int64_t count;
+};
+Status PeerAllReduceAddStep(void* ctx, cudaStream_t s) noexcept {
+    auto* a = static_cast<PeerAllReduceCtx*>(ctx);
+    return a->comm->AllReduceAddBf16(a->part, a->x, a->count, s);
+}
 
 }  // namespace
 }  // namespace aethermind
@@ -581,6 +592,17 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
             }
             AM_RETURN_IF_ERROR(pb.Add(OpType::kLinear, lin, {in}, {MView2(s->part.data(), A, M, H, H)}, &store, &W.w,
                                       p + name + "_partial"));
+            if (A == DType::kBF16 && m->rt->comm.OneShotReady(M * H)) {
+                auto pctx = std::make_shared<PeerAllReduceCtx>(
+                        PeerAllReduceCtx{&m->rt->comm, s->part.data(), s->x.data(), M * H});
+                ExecutionStep st;
+                st.label = p + name + "_allreduce_residual(peer)";
+                st.host_fn = PeerAllReduceAddStep;
+                st.host_ctx = pctx.get();
+                plan.steps.push_back(std::move(st));
+                plan.host_ctx_owned.push_back(std::move(pctx));
+                return Status::Ok();
+            }
             auto ctx = std::make_shared<AllReduceCtx>(AllReduceCtx{&m->rt->comm, s->part.data(), (size_t)(M * H)});
             ExecutionStep st;
             st.label = p + name + "_allreduce";
@@ -812,6 +834,19 @@ void am_runtime_destroy(am_runtime_t rt) {
     if (!rt) return;
     if (rt->stream) cudaStreamDestroy(rt->stream);
     delete rt;
+}
+
+am_status_code am_runtime_peer_handle(am_runtime_t rt, void* out64) {
+    if (!rt || !out64) return Fail(Status::InvalidArgument("am_runtime_peer_handle: null argument"));
+    Status s = rt->comm.PeerHandle(out64);
+    return s.ok() ? AM_STATUS_OK : Fail(s);
+}
+
+am_status_code am_runtime_open_peers(am_runtime_t rt, const void* handles) {
+    if (!rt || !handles) return Fail(Status::InvalidArgument("am_runtime_open_peers: null argument"));
+    if (cudaSetDevice(rt->device) != cudaSuccess) return Fail(Status::Internal("cudaSetDevice failed"));
+    Status s = rt->comm.OpenPeers(handles);
+    return s.ok() ? AM_STATUS_OK : Fail(s);
 }
 
 am_status_code am_nccl_get_unique_id(void* out128) {

@@ -75,6 +75,18 @@ class Runtime:
         self.h = h
         self.tp_rank, self.tp_size = tp_rank, tp_size
 
+    def peer_handle(self) -> bytes:
+        """This rank's 64-byte CUDA IPC handle of its all-reduce exchange area."""
+        buf = C.create_string_buffer(64)
+        L.check(lib().am_runtime_peer_handle(self.h, buf), "am_runtime_peer_handle")
+        return buf.raw
+
+    def open_peers(self, handles: list[bytes]) -> None:
+        """Opens every rank's exchange area (handles in rank order): decode steps
+        of sessions created afterwards all-reduce over peer memory."""
+        blob = C.create_string_buffer(b"".join(handles), 64 * len(handles))
+        L.check(lib().am_runtime_open_peers(self.h, blob), "am_runtime_open_peers")
+
     def close(self):
         if getattr(self, "h", None):
             lib().am_runtime_destroy(self.h)

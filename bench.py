@@ -253,6 +253,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="debug: fewer layers (invalidates the number)")
+    ap.add_argument("--nccl-allreduce", action="store_true", help="TP: NCCL for every all-reduce (no peer-memory one-shot)")
     ap.add_argument("--op", default=None, help="time one kernel instead: gemv_gate_up | gemm_gate_up")
     ap.add_argument("--copies", type=int, default=None, help="--op gemv_gate_up: weight copies rotated")
     ap.add_argument("--reps", type=int, default=None, help="--op: timed launches")
@@ -288,6 +289,11 @@ def main() -> None:
     if args.layers:
         cfg = dataclasses.replace(cfg, layers=args.layers)
     rt = session.Runtime(local, rank, world, nccl_id)
+    if world > 1 and not args.nccl_allreduce:
+        # decode all-reduces over peer memory: share the ranks' CUDA IPC handles
+        handles = [None] * world
+        dist.all_gather_object(handles, rt.peer_handle())
+        rt.open_peers(handles)
     model = session.Model(rt, cfg)
     model.init_synthetic(SEED)
     sess = session.Session(model)
@@ -330,6 +336,8 @@ def main() -> None:
         "data": "synthetic (seeded integer-hash INT4 weights, uniform token ids)",
         "config": {"workload": "llama3-8b-shape W4 g128 bs=1: prefill 512 + 256 greedy decode", "global_batch": 1,
                    "seq_len": PROMPT + NEW, "parallelism": f"tp{world}",
+                   "allreduce": "none" if world == 1 else ("nccl" if args.nccl_allreduce else
+                                                           "peer-memory one-shot (decode), nccl (prefill)"),
                    "l2": "weights (3.9 GB) exceed L2; no flush needed", "layers": cfg.layers},
         "prefill_tok_s": round(args.steps * PROMPT / (pre_total / 1e3), 1),
         "decode_ms_per_token": round(dec_total / decoded, 4),

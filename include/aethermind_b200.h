@@ -479,6 +479,15 @@ am_status_code am_session_last_gaps(am_session_t session, float* gaps, size_t ca
 /* Tensor parallelism: rank 0 creates the 128-byte NCCL unique id and shares it
  * with the other ranks (any transport) before am_runtime_create. */
 am_status_code am_nccl_get_unique_id(void* out128);
+/* One-shot all-reduce over peer memory for the decode steps (no counterpart
+ * in the reference, whose engine runs on one device). After am_runtime_create
+ * with tp_size > 1, every rank exports its exchange area as a 64-byte CUDA IPC
+ * handle, the ranks share them (any transport), and each rank opens the
+ * others' with the tp_size x 64 bytes in rank order. Sessions created
+ * afterwards reduce the o/down partials of messages up to 65536 elements with
+ * one kernel (sum + residual add) instead of NCCL + an add. Same node only. */
+am_status_code am_runtime_peer_handle(am_runtime_t runtime, void* out64);
+am_status_code am_runtime_open_peers(am_runtime_t runtime, const void* handles);
 /* Message of the last failing am_* session call on this thread. */
 const char* am_last_error(void);
 /* Diagnostics: number of registered CUDA kernels, and the resolved kernel of

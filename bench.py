@@ -192,14 +192,82 @@ def op_bench(args) -> None:
     print(json.dumps({"op": args.op, **r}), flush=True)
 
 
-def decode_bytes_per_token(cfg, ctx: float) -> float:
+def decode_bytes_per_token(cfg, ctx: float, batch: int = 1) -> float:
+    """HBM bytes of one decode step: every linear weight and its scales once
+    (lm_head included; a tied lm_head counted once, as INT8 rows) plus each
+    sequence's KV cache up to ctx."""
+    from aethermind_b200 import _lib as L
     H, I, d = cfg.hidden, cfg.inter, cfg.head_dim
     qkv = (cfg.n_q_heads + 2 * cfg.n_kv_heads) * d
     per_layer = H * qkv + cfg.n_q_heads * d * H + 2 * I * H + I * H
+    rows = cfg.layers * (qkv + H + 2 * I + H) + cfg.vocab
     params = cfg.layers * per_layer + cfg.vocab * H
-    w = params / 2 + params / 128 * 2
-    kv = cfg.layers * 2 * cfg.n_kv_heads * d * 2 * ctx
+    if cfg.weight_format == L.WFMT_INT8:
+        w = params + rows * 4
+    else:
+        w = params / 2 + params / 128 * 2
+    kv = cfg.layers * 2 * cfg.n_kv_heads * d * 2 * ctx * batch
     return w + kv
+
+
+def timed_generate(sess, prompt, new: int, dist) -> tuple[float, float]:
+    """One generate call; (prefill ms, decode ms) on the device, max over ranks."""
+    import torch
+    sess.generate(prompt, new)
+    p, d, _ = sess.timing()
+    if dist:
+        t = torch.tensor([p, d], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        p, d = t.tolist()
+    return p, d
+
+
+def extra_configs(sess, model_cfg, rt, world: int, dist, hbm_peak: float, tc_peak: float) -> dict:
+    """The other BASELINE workloads, one timed generate each after a short
+    warm-up: the 8B model at batch 8, the 1B W8 model (one GPU: replicas
+    only) and the 70B W4 model (tensor parallel over all ranks)."""
+    import dataclasses
+
+    import numpy as np
+
+    from aethermind_b200 import session
+    out = {}
+    rng = np.random.default_rng(SEED + 1)
+    # 8B W4, batch 8, 512-token prompts, 256 tokens
+    p8 = rng.integers(0, model_cfg.vocab, (8, PROMPT)).astype(np.uint32)
+    sess.generate(p8, 4)
+    pre, dec = timed_generate(sess, p8, NEW, dist)
+    bpt = decode_bytes_per_token(model_cfg, PROMPT + NEW / 2, 8) / world
+    out["8b_w4_bs8"] = {"decode_tok_s": round(8 * (NEW - 1) / (dec / 1e3), 1),
+                        "prefill_tok_s": round(8 * PROMPT / (pre / 1e3), 1),
+                        "decode_hbm_frac_per_gpu": round(bpt * (NEW - 1) / (dec / 1e3) / 1e9 / hbm_peak, 3)}
+    # 1B W8 (tied embeddings), 128-token prompt, 128 tokens, one GPU
+    if world == 1:
+        c1 = dataclasses.replace(session.LLAMA_1B_W8, max_seq=2048)
+        m1 = session.Model(rt, c1)
+        m1.init_synthetic(SEED)
+        s1 = session.Session(m1)
+        pr = rng.integers(0, c1.vocab, 128).astype(np.uint32)
+        s1.generate(pr, 4)
+        pre, dec = timed_generate(s1, pr, 128, None)
+        bpt = decode_bytes_per_token(c1, 128 + 64)
+        out["1b_w8"] = {"decode_tok_s": round(127 / (dec / 1e3), 1), "prefill_tok_s": round(128 / (pre / 1e3), 1),
+                        "decode_hbm_frac": round(bpt * 127 / (dec / 1e3) / 1e9 / hbm_peak, 3)}
+        del s1, m1
+    # 70B W4, 2048-token prompt, 256 tokens, TP over all ranks
+    c7 = dataclasses.replace(session.LLAMA_70B_W4, max_seq=4096)
+    m7 = session.Model(rt, c7)
+    m7.init_synthetic(SEED)
+    s7 = session.Session(m7)
+    pr = rng.integers(0, c7.vocab, 2048).astype(np.uint32)
+    s7.generate(pr[:64], 4)
+    pre, dec = timed_generate(s7, pr, NEW, dist)
+    bpt = decode_bytes_per_token(c7, 2048 + NEW / 2) / world
+    out["70b_w4"] = {"decode_tok_s": round((NEW - 1) / (dec / 1e3), 2), "prefill_tok_s": round(2048 / (pre / 1e3), 1),
+                     "decode_hbm_frac_per_gpu": round(bpt * (NEW - 1) / (dec / 1e3) / 1e9 / hbm_peak, 3),
+                     "tp": world}
+    del s7, m7
+    return out
 
 
 def cpu_oracle_model(cfg):
@@ -253,6 +321,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="debug: fewer layers (invalidates the number)")
+    ap.add_argument("--no-extra", action="store_true", help="skip the other BASELINE workloads (bs=8, 1B W8, 70B W4)")
     ap.add_argument("--nccl-allreduce", action="store_true", help="TP: NCCL for every all-reduce (no peer-memory one-shot)")
     ap.add_argument("--op", default=None, help="time one kernel instead: gemv_gate_up | gemm_gate_up")
     ap.add_argument("--copies", type=int, default=None, help="--op gemv_gate_up: weight copies rotated")
@@ -285,7 +354,7 @@ def main() -> None:
         dist.broadcast_object_list(obj, src=0)
         nccl_id = obj[0]
 
-    cfg = dataclasses.replace(session.LLAMA_8B_W4, max_seq=4096)
+    cfg = dataclasses.replace(session.LLAMA_8B_W4, max_seq=4096, max_batch=8)
     if args.layers:
         cfg = dataclasses.replace(cfg, layers=args.layers)
     rt = session.Runtime(local, rank, world, nccl_id)
@@ -364,6 +433,8 @@ def main() -> None:
         line["gpu_launches"] = args.steps * (launches(pre_steps) + (NEW - 1) * launches(dec_steps))
     except Exception as e:  # pragma: no cover
         line["gpu_launches_error"] = str(e)
+    if not args.no_extra:
+        line["configs"] = extra_configs(sess, cfg, rt, world, dist, hbm_peak, tc_peak)
     if rank == 0 and world == 1 and not args.no_roofline:
         del sess, model
         torch.cuda.empty_cache()

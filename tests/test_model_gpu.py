@@ -58,7 +58,7 @@ def _small(cfg_name, sess_mod, layers=2):
     return dataclasses.replace(base, layers=layers, max_seq=256, max_batch=2)
 
 
-@pytest.mark.parametrize("cfg_name", ["LLAMA_8B_W4", "LLAMA_1B_W8"])
+@pytest.mark.parametrize("cfg_name", ["LLAMA_8B_W4", "LLAMA_1B_W8", "LLAMA_70B_W4"])
 def test_quantized_model_matches_oracle(sess_mod, rt, oracle_lib, cfg_name):
     cfg = _small(cfg_name, sess_mod)
     m = sess_mod.Model(rt, cfg)

@@ -93,9 +93,11 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.rows)}
 
 
-def gemv_roofline(hbm_peak: float, ncopy: int | None = None, reps: int | None = None) -> dict:
-    """Times the W4 GEMV of the 8B gate/up projection (N = 2 x 14336, K = 4096)
-    alone, rotating over enough weight copies that every launch reads HBM."""
+def gemv_roofline(hbm_peak: float, ncopy: int | None = None, reps: int | None = None, m: int = 1,
+                  shape: str = "gate_up") -> dict:
+    """Times the W4 GEMV of the 8B gate/up projection (N = 2 x 14336, K = 4096;
+    shape "down": N = 4096, K = 14336) alone for m activation rows, rotating
+    over enough weight copies that every launch reads HBM."""
     import ctypes as C
 
     import torch
@@ -103,15 +105,15 @@ def gemv_roofline(hbm_peak: float, ncopy: int | None = None, reps: int | None = 
     from aethermind_b200 import _lib as L
     from aethermind_b200 import ops
 
-    n, k = 2 * 14336, 4096
+    n, k = (2 * 14336, 4096) if shape == "gate_up" else (4096, 14336)
     q, s = ops.synth_w4(SEED, 99, n, k, 0.004)
     copies = []
     per = n * k // 2 + n * (k // 128) * 2
     ncopy = ncopy or max(2, int(512e6 // per) + 1)  # > 4 x L2
     for _ in range(ncopy):
         copies.append(ops.prepack(L.WFMT_INT4, q, s, n, k))
-    x = torch.randn(1, k, device="cuda").to(torch.bfloat16)
-    y = torch.empty(1, n, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    y = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
     args = []
     for pw in copies:
         a, _, _ = ops._linear_args(x, pw, L.EPI_STORE, None, y)
@@ -129,15 +131,15 @@ def gemv_roofline(hbm_peak: float, ncopy: int | None = None, reps: int | None = 
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / reps
-    alg = n * k // 2 + n * (k // 128) * 2 + k * 2 + n * 2
+    alg = n * k // 2 + n * (k // 128) * 2 + m * (k * 2 + n * 2)
     gbs = alg / (us * 1e-6) / 1e9
     del copies
     torch.cuda.empty_cache()
-    return {"kernel": "gemv_tc_kernel<INT4> (8B gate_up, n=28672 k=4096, m=1)", "bound": "hbm",
+    return {"kernel": f"gemv_tc_kernel<INT4> (8B {shape}, n={n} k={k}, m={m})", "bound": "hbm",
             "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(gbs / hbm_peak, 3),
             # dram__bytes_read.sum + dram__bytes_write.sum of one launch of this kernel and shape,
             # from the ncu capture summarised in profiles/gemv_w4_gate_up_8b.md
-            "traffic": GEMV_GATE_UP_TRAFFIC, "alg_bytes_per_launch": alg, "us_per_launch": round(us, 2)}
+            "traffic": GEMV_GATE_UP_TRAFFIC if (shape, m) == ("gate_up", 1) else None, "alg_bytes_per_launch": alg, "us_per_launch": round(us, 2)}
 
 
 GEMV_GATE_UP_TRAFFIC = 60635904
@@ -183,8 +185,8 @@ def op_bench(args) -> None:
     import torch
     torch.cuda.set_device(0)
     hbm_peak, tc_peak, _ = _peaks()
-    if args.op == "gemv_gate_up":
-        r = gemv_roofline(hbm_peak, ncopy=args.copies, reps=args.reps)
+    if args.op in ("gemv_gate_up", "gemv_down"):
+        r = gemv_roofline(hbm_peak, ncopy=args.copies, reps=args.reps, m=args.m, shape=args.op[5:])
     elif args.op == "gemm_gate_up":
         r = gemm_prefill_timing(tc_peak, reps=args.reps or 20)
     else:
@@ -323,8 +325,9 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=None, help="debug: fewer layers (invalidates the number)")
     ap.add_argument("--no-extra", action="store_true", help="skip the other BASELINE workloads (bs=8, 1B W8, 70B W4)")
     ap.add_argument("--nccl-allreduce", action="store_true", help="TP: NCCL for every all-reduce (no peer-memory one-shot)")
-    ap.add_argument("--op", default=None, help="time one kernel instead: gemv_gate_up | gemm_gate_up")
-    ap.add_argument("--copies", type=int, default=None, help="--op gemv_gate_up: weight copies rotated")
+    ap.add_argument("--op", default=None, help="time one kernel instead: gemv_gate_up | gemv_down | gemm_gate_up")
+    ap.add_argument("--copies", type=int, default=None, help="--op gemv_*: weight copies rotated")
+    ap.add_argument("--m", type=int, default=1, help="--op gemv_*: activation rows")
     ap.add_argument("--reps", type=int, default=None, help="--op: timed launches")
     args = ap.parse_args()
     if args.op:

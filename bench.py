@@ -361,11 +361,29 @@ def main() -> None:
     if args.layers:
         cfg = dataclasses.replace(cfg, layers=args.layers)
     rt = session.Runtime(local, rank, world, nccl_id)
+    peer_error = None
     if world > 1 and not args.nccl_allreduce:
         # decode all-reduces over peer memory: share the ranks' CUDA IPC handles
+        # (every rank must agree: any failure keeps all ranks on NCCL)
+        try:
+            mine = rt.peer_handle()
+        except Exception as e:  # pragma: no cover - depends on the box
+            mine, peer_error = None, f"peer_handle: {e}"
         handles = [None] * world
-        dist.all_gather_object(handles, rt.peer_handle())
-        rt.open_peers(handles)
+        dist.all_gather_object(handles, mine)
+        if all(h is not None for h in handles):
+            try:
+                rt.open_peers(handles)
+                ok = 1
+            except Exception as e:  # pragma: no cover
+                ok, peer_error = 0, f"open_peers: {e}"
+            flags = [None] * world
+            dist.all_gather_object(flags, ok)
+            if not all(flags):
+                raise SystemExit(f"rank {rank}: peer all-reduce setup failed on a rank ({peer_error}); "
+                                 "rerun with --nccl-allreduce")
+        else:
+            args.nccl_allreduce = True
     model = session.Model(rt, cfg)
     model.init_synthetic(SEED)
     sess = session.Session(model)
@@ -436,8 +454,13 @@ def main() -> None:
         line["gpu_launches"] = args.steps * (launches(pre_steps) + (NEW - 1) * launches(dec_steps))
     except Exception as e:  # pragma: no cover
         line["gpu_launches_error"] = str(e)
+    if peer_error:
+        line["allreduce_note"] = peer_error
     if not args.no_extra:
-        line["configs"] = extra_configs(sess, cfg, rt, world, dist, hbm_peak, tc_peak)
+        try:
+            line["configs"] = extra_configs(sess, cfg, rt, world, dist, hbm_peak, tc_peak)
+        except Exception as e:  # pragma: no cover - reported, the headline line stands
+            line["configs_error"] = f"{type(e).__name__}: {e}"
     if rank == 0 and world == 1 and not args.no_roofline:
         del sess, model
         torch.cuda.empty_cache()

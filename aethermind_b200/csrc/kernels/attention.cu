@@ -14,6 +14,8 @@
 // (max, sum, unnormalised o) partials and a combine kernel merges them.
 #include <mutex>
 
+#include <cstdlib>
+
 #include "../amcu_internal.h"
 #include "attn_decode.cuh"
 #include "common.cuh"
@@ -293,6 +295,10 @@ static bool dispatch_grp(const AttnKParams& p, int grp, int64_t rows, cudaStream
 
 }  // namespace amcu
 
+namespace amcu {
+bool launch_attn_prefill_flash(const AmcuAttentionArgs* a, cudaStream_t s);
+}  // namespace amcu
+
 using namespace amcu;
 
 namespace {
@@ -387,6 +393,13 @@ am_status_code amcu_attn_prefill(const AmcuAttentionArgs* a, void* stream) {
     am_status_code st = validate_attn(a, "amcu_attn_prefill");
     if (st != AM_STATUS_OK) return st;
     if (a->rows == 0) return AM_STATUS_OK;
+    // bf16: the tensor-core flash kernel (attention_prefill.cu); fp32 and any
+    // shape it does not take: one CTA per (row, kv head)
+    static const bool flash = [] {
+        const char* v = std::getenv("AMCU_ATTN_PREFILL_FLASH");
+        return !(v && v[0] == '0');
+    }();
+    if (flash && launch_attn_prefill_flash(a, as_stream(stream))) return check_launch("amcu_attn_prefill");
     return run_attn(a, 1, as_stream(stream));
 }
 

@@ -384,6 +384,26 @@ def test_attention_prefill_causal(ops, orc, dtype):
         np.testing.assert_allclose(to_np(out), ref, rtol=F32_RTOL, atol=1e-5)
 
 
+@pytest.mark.parametrize("nq,nkv,d,R,B", [(32, 8, 128, 130, 1), (32, 8, 64, 64, 2), (64, 8, 128, 200, 2),
+                                         (8, 8, 64, 17, 1)])
+def test_attention_prefill_shapes(ops, orc, nq, nkv, d, R, B):
+    """Prefill attention (bf16: the tensor-core flash kernel) over ragged row
+    counts, head_dim 64 and 128, GQA groups 1/4/8 and two sequences with
+    different start positions, against the oracle sequence by sequence."""
+    cap = 512
+    rng = np.random.default_rng(R + d)
+    p0s = [5, 100][:B]
+    q = orc.bf16_round(rng.normal(0, 1, (B * R, nq * d)).astype(np.float32))
+    kc = orc.bf16_round(rng.normal(0, 1, (B, nkv, cap, d)).astype(np.float32))
+    vc = orc.bf16_round(rng.normal(0, 1, (B, nkv, cap, d)).astype(np.float32))
+    out = ops.attention(bf16_dev(q), bf16_dev(kc), bf16_dev(vc), torch.tensor(p0s, dtype=torch.int32, device="cuda"),
+                        R, nq, nkv, d, decode=False)
+    got = to_np(out)
+    for b in range(B):
+        ref = orc.attention(q[b * R:(b + 1) * R], kc[b], vc[b], p0s[b], nq, nkv, d, bf=True)
+        np.testing.assert_allclose(got[b * R:(b + 1) * R], ref, rtol=BF_RTOL, atol=BF_ATOL)
+
+
 # ------------------------------------------------------------- elementwise
 @pytest.mark.parametrize("nq,nkv,d", [(32, 8, 128), (32, 8, 64), (16, 8, 128), (8, 8, 64)])
 def test_fused_rope_attention_matches_two_step_path(ops, orc, nq, nkv, d):

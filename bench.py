@@ -44,6 +44,8 @@ SEED = 0
 METRIC = "decode tok/s bs=1 (8B W4 g128, 512-token prompt, 256 greedy tokens)"
 
 
+WORKLOAD = "llama3-8b-shape W4 g128 bs=1: prefill 512 + 256 greedy decode"
+
 def _peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -305,8 +307,9 @@ def run_reference(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * 2 / v, 1),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded integer-hash INT4 weights, uniform token ids)",
-            "config": {"workload": "llama3-8b-shape W4 g128 bs=1 decode", "global_batch": 1, "seq_len": PROMPT + NEW,
-                       "parallelism": "cpu"},
+            # the GPU arm's config (the timed CPU work is a bounded sample of it, see cpu_baseline.sample)
+            "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": PROMPT + NEW,
+                       "parallelism": f"tp{args.gpus}", "layers": cfg.layers},
             "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
                              "sample": "per step: 8-token prompt prefill + 2 greedy decode tokens of the full 32-layer "
                                        "8B W4 model; decode tok/s (CPU restatement in oracle/am_oracle.c, OpenMP)"},
@@ -424,7 +427,7 @@ def main() -> None:
         "warmup": args.warmup, "ms_per_step": round((dec_total + pre_total) / args.steps, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded integer-hash INT4 weights, uniform token ids)",
-        "config": {"workload": "llama3-8b-shape W4 g128 bs=1: prefill 512 + 256 greedy decode", "global_batch": 1,
+        "config": {"workload": WORKLOAD, "global_batch": 1,
                    "seq_len": PROMPT + NEW, "parallelism": f"tp{world}",
                    "allreduce": "none" if world == 1 else ("nccl" if args.nccl_allreduce else
                                                            "peer-memory one-shot (decode), nccl (prefill)"),

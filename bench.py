@@ -42,9 +42,8 @@ PROMPT = 512
 NEW = 256
 SEED = 0
 METRIC = "decode tok/s bs=1 (8B W4 g128, 512-token prompt, 256 greedy tokens)"
-
-
 WORKLOAD = "llama3-8b-shape W4 g128 bs=1: prefill 512 + 256 greedy decode"
+
 
 def _peaks():
     p = ROOT / "MEASURED_PEAKS.json"

@@ -313,10 +313,14 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
 
 template <int FMT>
 static int stage_units(int64_t k) {
-    // group units per stage: the largest divisor of k/128 that keeps a stage
-    // at most kMaxStageBytes (INT4: 16 pair records = 16.5 KB; INT8: 8 tile
-    // pairs = 16 KB)
-    const int G = (int)(k / 128), cap = FMT == AMCU_WFMT_INT4 ? 16 : 8;
+    // group units per stage: the largest divisor of k/128 up to a cap (INT4:
+    // 32 pair records = 33 KB, so a consumer warp takes 4 records between two
+    // ring waits -- measured 2.8% faster decode than 16; INT8: 8 tile pairs =
+    // 16 KB)
+#ifndef GEMV_W4_SU_CAP
+#define GEMV_W4_SU_CAP 32
+#endif
+    const int G = (int)(k / 128), cap = FMT == AMCU_WFMT_INT4 ? GEMV_W4_SU_CAP : 8;
     int best = 1;
     for (int d = 1; d <= cap; ++d)
         if (G % d == 0) best = d;

@@ -143,7 +143,7 @@ def gemv_roofline(hbm_peak: float, ncopy: int | None = None, reps: int | None = 
             "traffic": GEMV_GATE_UP_TRAFFIC if (shape, m) == ("gate_up", 1) else None, "alg_bytes_per_launch": alg, "us_per_launch": round(us, 2)}
 
 
-GEMV_GATE_UP_TRAFFIC = 60635904
+GEMV_GATE_UP_TRAFFIC = 60764416
 
 
 def gemm_prefill_timing(tc_peak: float, reps: int = 20) -> dict:

@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
 }
 
 template <int FMT>
-static int stage_units(int64_t k) {
+static int stage_units(int64_t k, int cap_w4 = 0) {
     // group units per stage: the largest divisor of k/128 up to a cap (INT4:
     // 32 pair records = 33 KB, so a consumer warp takes 4 records between two
     // ring waits -- measured 2.8% faster decode than 16; INT8: 8 tile pairs =
@@ -320,7 +320,7 @@ static int stage_units(int64_t k) {
 #ifndef GEMV_W4_SU_CAP
 #define GEMV_W4_SU_CAP 32
 #endif
-    const int G = (int)(k / 128), cap = FMT == AMCU_WFMT_INT4 ? GEMV_W4_SU_CAP : 8;
+    const int G = (int)(k / 128), cap = FMT == AMCU_WFMT_INT4 ? (cap_w4 > 0 ? cap_w4 : GEMV_W4_SU_CAP) : 8;
     int best = 1;
     for (int d = 1; d <= cap; ++d)
         if (G % d == 0) best = d;
@@ -369,11 +369,14 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
         cudaFuncSetAttribute(gemv_tc_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
     }
     constexpr int UB = FMT == AMCU_WFMT_INT4 ? kW4PairBytes : 2048;
-    const int su = stage_units<FMT>(p.k);
+    const int per_cta = smem_per_sm / GEMV_CPS - 2048;  // room for the per-CTA reserve
+    int su = stage_units<FMT>(p.k);
+    // long rows (one activation row of K above ~24K columns): the large stages
+    // would leave room for one CTA per SM, so they go back to 16 records
+    if (FMT == AMCU_WFMT_INT4 && gemv_smem<FMT>(1, p.k, su * UB, 2).total > per_cta) su = stage_units<FMT>(p.k, 16);
     const int sby = su * UB;
     // Ring stages: as many (2..8) as keep GEMV_CPS CTAs resident per SM with
     // one activation row.
-    const int per_cta = smem_per_sm / GEMV_CPS - 2048;  // room for the per-CTA reserve
     int stages = 8;
     while (stages > 2 && gemv_smem<FMT>(1, p.k, sby, stages).total > per_cta) --stages;
     p.stages = stages;

@@ -80,6 +80,21 @@ def test_quantized_model_matches_oracle(sess_mod, rt, oracle_lib, cfg_name):
     np.testing.assert_array_equal(gb[1], s.generate(p2[1], 8))
 
 
+def test_batch8_rows_equal_single_runs(sess_mod, rt):
+    """Batch 8 (the decode GEMVs' largest m: the down projection's 8 rows of
+    K = 14336 go in two row slices) gives every sequence the tokens it gets
+    alone."""
+    import dataclasses
+    cfg = dataclasses.replace(sess_mod.LLAMA_8B_W4, layers=2, max_seq=128, max_batch=8)
+    m = sess_mod.Model(rt, cfg)
+    m.init_synthetic(seed=4)
+    s = sess_mod.Session(m)
+    p8 = np.random.default_rng(13).integers(0, cfg.vocab, (8, 12)).astype(np.uint32)
+    got = s.generate(p8, 6)
+    for i in range(8):
+        np.testing.assert_array_equal(got[i], s.generate(p8[i], 6))
+
+
 def test_persistent_decode_matches_per_op_plan(sess_mod, rt, oracle_lib):
     """The persistent decode step (one launch for all layers, bs <= 2, INT4)
     against the per-op decode plan and the oracle: same tokens up to a

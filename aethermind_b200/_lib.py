@@ -23,7 +23,8 @@ STATUS_NAMES = [
     "PERMISSION_DENIED", "RESOURCE_EXHAUSTED", "FAILED_PRECONDITION", "ABORTED", "OUT_OF_RANGE",
     "UNIMPLEMENTED", "INTERNAL", "UNAVAILABLE", "DATA_LOSS", "OVERFLOW", "UNAUTHENTICATED",
 ]
-OK, INVALID_ARGUMENT, NOT_FOUND, FAILED_PRECONDITION, OUT_OF_RANGE, UNIMPLEMENTED = 0, 3, 5, 9, 11, 12
+OK, INVALID_ARGUMENT, DEADLINE_EXCEEDED, NOT_FOUND, FAILED_PRECONDITION, OUT_OF_RANGE, UNIMPLEMENTED = \
+    0, 3, 4, 5, 9, 11, 12
 
 
 class AmError(RuntimeError):
@@ -100,6 +101,11 @@ class AmSessionConfig(C.Structure):
                 ("persistent_decode", C.c_int32)]
 
 
+class AmcuAllReduceArgs(C.Structure):
+    _fields_ = [("part", C.c_void_p), ("x", C.c_void_p), ("n", C.c_int64), ("rank", C.c_int32),
+                ("world", C.c_int32), ("areas", C.c_void_p * 8), ("wait_limit_us", C.c_uint64)]
+
+
 P = C.c_void_p
 _SIGS = {
     "amcu_last_error": (C.c_char_p, []),
@@ -141,6 +147,8 @@ _SIGS = {
     "amcu_argmax_workspace_bytes": (C.c_size_t, [C.c_int64]),
     "amcu_argmax_ws": (C.c_int, [P, C.c_int64, C.c_int64, C.c_int64, C.c_int32, P, P, P, C.c_size_t, P]),
     "amcu_embedding": (C.c_int, [C.POINTER(AmcuEmbeddingArgs), P]),
+    "amcu_allreduce_area_bytes": (C.c_size_t, []),
+    "amcu_allreduce_oneshot_add": (C.c_int, [C.POINTER(AmcuAllReduceArgs), P]),
     "am_runtime_create": (P, [C.POINTER(AmConfig)]),
     "am_runtime_destroy": (None, [P]),
     "am_nccl_get_unique_id": (C.c_int, [P]),

@@ -53,6 +53,13 @@ inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
     cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
+// cudaFuncSetAttribute(func, attr, value) once per (device, function,
+// attribute) on the current device: function attributes are per device, so a
+// process that runs on several devices sets them on each (thread-safe).
+void set_func_attr_once(const void* func, cudaFuncAttribute attr, int value);
+// Shared memory per SM of the current device (cached per device).
+int smem_per_sm();
+
 // Per-device int32 error word that kernels with bounded waits write on timeout
 // (allocated on first use on the current device; nullptr if that fails).
 int32_t* device_error_word();

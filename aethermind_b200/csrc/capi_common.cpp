@@ -6,6 +6,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <set>
+#include <tuple>
 
 #include <dlfcn.h>
 #include <execinfo.h>
@@ -46,6 +48,27 @@ bool pdl_enabled() {
         return !(v && v[0] == '0');
     }();
     return on;
+}
+
+void set_func_attr_once(const void* func, cudaFuncAttribute attr, int value) {
+    static std::mutex mu;
+    static std::set<std::tuple<int, const void*, int>> done;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.insert({dev, func, (int)attr}).second) cudaFuncSetAttribute(func, attr, value);
+}
+
+int smem_per_sm() {
+    static int per_dev[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 228 * 1024;
+    if (per_dev[dev] == 0) {  // benign race: every writer stores the same value
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        per_dev[dev] = v > 0 ? v : 228 * 1024;
+    }
+    return per_dev[dev];
 }
 
 int32_t* device_error_word() {

@@ -32,6 +32,13 @@ namespace amcu {
 
 constexpr int32_t kErrArWait = 0x401;
 constexpr int kArThreads = 256;
+constexpr uint64_t kArDefaultWaitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -71,9 +78,10 @@ __global__ void __launch_bounds__(kArThreads) ar_oneshot_add_kernel(ArParams p) 
     // 3. wait for the peers' chunks
     if (tid < p.world && tid != p.rank) {
         const uint32_t* f = reinterpret_cast<const uint32_t*>(own + ar_flags_offset()) + tid * kArMaxCtas + c;
-        const long long t0 = clock64();
+        const uint64_t t0 = globaltimer_ns();
+        const uint64_t lim = p.wait_ns ? p.wait_ns : kArDefaultWaitNs;
         while ((int32_t)(ld_acquire_sys(f) - e) < 0) {
-            if (clock64() - t0 > kSpinLimitCycles) {
+            if (globaltimer_ns() - t0 > lim) {
                 record_device_error(p.err, kErrArWait);
                 break;
             }
@@ -127,3 +135,33 @@ void launch_ar_oneshot_add(const ArParams& p, cudaStream_t s) {
 }
 
 }  // namespace amcu
+
+using namespace amcu;
+
+extern "C" size_t amcu_allreduce_area_bytes(void) { return ar_area_bytes(); }
+
+extern "C" am_status_code amcu_allreduce_oneshot_add(const AmcuAllReduceArgs* a, void* stream) {
+    AMCU_REQUIRE(a != nullptr, "amcu_allreduce_oneshot_add: null args");
+    AMCU_REQUIRE(a->world >= 2 && a->world <= kArMaxRanks, "amcu_allreduce_oneshot_add: world must be in [2, %d]",
+                 kArMaxRanks);
+    AMCU_REQUIRE(a->rank >= 0 && a->rank < a->world, "amcu_allreduce_oneshot_add: rank out of range");
+    AMCU_REQUIRE(ar_oneshot_supported(a->n, a->world),
+                 "amcu_allreduce_oneshot_add: n must be a positive multiple of 8 up to %lld",
+                 (long long)kArMaxElems);
+    AMCU_REQUIRE(a->part && a->x && aligned(a->part, 16) && aligned(a->x, 16),
+                 "amcu_allreduce_oneshot_add: part and x must be 16-byte aligned device pointers");
+    ArParams p{};
+    p.part = a->part;
+    p.x = a->x;
+    p.n = a->n;
+    p.rank = a->rank;
+    p.world = a->world;
+    for (int r = 0; r < a->world; ++r) {
+        AMCU_REQUIRE(a->areas[r] && aligned(a->areas[r], 16), "amcu_allreduce_oneshot_add: area %d missing", r);
+        p.area[r] = static_cast<uint8_t*>(a->areas[r]);
+    }
+    p.err = device_error_word();
+    p.wait_ns = a->wait_limit_us * 1000ull;
+    launch_ar_oneshot_add(p, as_stream(stream));
+    return check_launch("amcu_allreduce_oneshot_add");
+}

@@ -18,6 +18,7 @@ struct ArParams {
     int rank, world;
     uint8_t* area[kArMaxRanks];     // every rank's exchange area as mapped in this process (own included)
     int32_t* err;
+    uint64_t wait_ns;               // bound of the wait for the peers' chunks (0: about 2 s)
 };
 
 size_t ar_area_bytes();

@@ -136,11 +136,7 @@ template <int GRP, int D, int CS>
 static cudaError_t launch_rope_attn(const RopeAttnParams& p, int64_t nkv, int64_t rows, cudaStream_t s) {
     constexpr int cs = CS;
     auto kern = attn_rope_decode_kernel<GRP, D, CS>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        attr_set = true;
-    }
+    set_func_attr_once((const void*)kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)cs, (unsigned)nkv, (unsigned)rows);
     cfg.blockDim = dim3(kRaThreads);
@@ -164,7 +160,7 @@ static int cluster_size() {
     static int cs = 0;
     if (cs == 0) {
         auto kern = attn_rope_decode_kernel<GRP, D, 16>;
-        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        set_func_attr_once((const void*)kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(16, 1, 1);
         cfg.blockDim = dim3(kRaThreads);

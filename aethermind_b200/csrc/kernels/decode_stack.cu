@@ -69,19 +69,26 @@ struct DsParams {
     int stages;
     int32_t *err, *status;
     int rbmax;     // most row blocks a CTA owns in any GEMV phase
-    int dbg_skip;  // diagnostics (AMCU_DS_SKIP): bit 0 skips attention, bit 1 the grid barriers, bit 2 the weight stream (wrong results)
-    unsigned long long* trace;  // diagnostics (AMCU_DS_TRACE): [cta][layer][kDsMarks] globaltimer stamps, or null
+    int dbg_skip;  // diagnostics, AMCU_DIAG builds only (AMCU_DS_SKIP): bit 0 skips attention, bit 1 the grid barriers, bit 2 the weight stream (wrong results)
+    unsigned long long* trace;  // diagnostics, AMCU_DIAG builds only (AMCU_DS_TRACE): [cta][layer][kDsMarks] globaltimer stamps, or null
 };
 
 constexpr int kDsMarks = 26;  // trace stamps per layer
+#ifdef AMCU_DIAG
+#define DS_SKIP(p) ((p).dbg_skip)
+#define DS_TRACE(p) ((p).trace)
+#else
+#define DS_SKIP(p) 0
+#define DS_TRACE(p) ((unsigned long long*)nullptr)
+#endif
 
 __device__ __forceinline__ void ds_mark(const DsParams& p, int l, int idx) {
-    if (p.trace && threadIdx.x == 0) {
+    if (DS_TRACE(p) && threadIdx.x == 0) {
         unsigned long long t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        p.trace[((size_t)blockIdx.x * p.nlayers + l) * kDsMarks + idx] = t;
+        DS_TRACE(p)[((size_t)blockIdx.x * p.nlayers + l) * kDsMarks + idx] = t;
         if (idx == 0 || idx == 18)  // SM clock cycles beside the layer's first and last stamps
-            p.trace[((size_t)blockIdx.x * p.nlayers + l) * kDsMarks + (idx == 0 ? 24 : 25)] = clock64();
+            DS_TRACE(p)[((size_t)blockIdx.x * p.nlayers + l) * kDsMarks + (idx == 0 ? 24 : 25)] = clock64();
     }
 }
 
@@ -115,7 +122,7 @@ __device__ __forceinline__ void st_relaxed_gpu(unsigned int* a, unsigned int v) 
 constexpr int kDsBarGroups = 16;
 constexpr int kDsBarWords = 32 * (2 + kDsBarGroups);  // gen, top, groups: one 128-byte line each
 __device__ __forceinline__ void ds_grid_barrier(const DsParams& p, bool& ok) {
-    if (p.dbg_skip & 2) return;
+    if (DS_SKIP(p) & 2) return;
     named_bar_sync(kBarGemv, kDsCT);
     if (threadIdx.x == 0) {
         unsigned int* gen = p.bar;
@@ -220,7 +227,7 @@ __device__ __noinline__ void ds_gemv(const DsParams& p, DsRing& r, int64_t n, in
     const int S = r.S;
     int slot = r.slot;
     uint32_t phase = r.phase;
-    const bool stream = !(p.dbg_skip & 4);
+    const bool stream = !(DS_SKIP(p) & 4);
     bool live = ok;
     for (int rb = lo; rb < hi; ++rb) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -426,7 +433,7 @@ __global__ void __maxnreg__(96) decode_stack_kernel(DsParams p) {
 
     if (warp == kDsConsumers) {
         // ---- producer: the CTA's share of every layer's weights, in consumption order
-        if (lane == 0 && !(p.dbg_skip & 4)) {
+        if (lane == 0 && !(DS_SKIP(p) & 4)) {
             int slot = 0;
             uint32_t phase = 0;
             int64_t i = 0;
@@ -475,7 +482,7 @@ __global__ void __maxnreg__(96) decode_stack_kernel(DsParams p) {
         ds_mark(p, l, 4);
         ds_grid_barrier(p, ok);
         ds_mark(p, l, 5);
-        if (!(p.dbg_skip & 1)) ds_attention<GRP, D>(p, ly, smem, L, ok, l);
+        if (!(DS_SKIP(p) & 1)) ds_attention<GRP, D>(p, ly, smem, L, ok, l);
         ds_mark(p, l, 6);
         ds_grid_barrier(p, ok);
         ds_mark(p, l, 7);
@@ -546,6 +553,7 @@ static am_status_code launch_stack(DsParams p, cudaStream_t s) {
         cudaGetLastError();
         return set_error(AM_STATUS_INTERNAL, "amcu_decode_stack launch: %s", cudaGetErrorString(e));
     }
+#ifdef AMCU_DIAG
     if (p.trace) {
         // diagnostics: append the stamps of this (eager, synchronised) step to the trace file
         const size_t n = (size_t)num_sms() * p.nlayers * kDsMarks;
@@ -560,6 +568,7 @@ static am_status_code launch_stack(DsParams p, cudaStream_t s) {
             }
         }
     }
+#endif
     return AM_STATUS_OK;
 }
 
@@ -618,12 +627,14 @@ am_status_code amcu_decode_stack(const AmcuDecodeStackArgs* a, void* stream) {
     p.ns = ns < 1 ? 1 : (ns > kDsMaxSplits ? kDsMaxSplits : ns);
     p.err = device_error_word();
     p.status = a->status;
+    p.dbg_skip = 0;
+    p.trace = nullptr;
+#ifdef AMCU_DIAG
     static const int dbg = [] {
         const char* v = std::getenv("AMCU_DS_SKIP");
         return v ? std::atoi(v) : 0;
     }();
     p.dbg_skip = dbg;
-    p.trace = nullptr;
     if (std::getenv("AMCU_DS_TRACE")) {
         // diagnostics only (eager sessions): one stamp buffer, grown on demand
         static unsigned long long* buf = nullptr;
@@ -641,6 +652,7 @@ am_status_code amcu_decode_stack(const AmcuDecodeStackArgs* a, void* stream) {
             p.trace = buf;
         }
     }
+#endif
     const int grp = (int)(a->n_q_heads / a->n_kv_heads);
     const cudaStream_t s = as_stream(stream);
     if (a->head_dim == 128 && grp == 4) return launch_stack<4, 128>(p, s);

@@ -57,9 +57,20 @@ struct GemmTcKParams {
               // bit 4 the activation loads, bit 5 the record loads (swapped kernel)
 };
 
+// Diagnostics (AMCU_DIAG builds only; the default build compiles them out):
+// ablation bits that skip parts of the work (wrong results, for timing
+// studies) and per-CTA timers.
+#ifdef AMCU_DIAG
+#define TC_DBG(p) ((p).dbg)
+#define TC_TRACE(p) ((p).trace)
+#else
+#define TC_DBG(p) 0
+#define TC_TRACE(p) ((unsigned long long*)nullptr)
+#endif
+
 // Diagnostics: a globaltimer stamp into slot `slot` of this CTA's counters.
 __device__ __forceinline__ void tc_stamp(const GemmTcKParams& p, int slot) {
-    if (!p.trace) return;
+    if (!TC_TRACE(p)) return;
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     p.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 16 + slot] = t;
@@ -69,10 +80,10 @@ __device__ __forceinline__ void tc_stamp(const GemmTcKParams& p, int slot) {
 struct TcClock {
     long long t0 = 0;
     __device__ __forceinline__ void start(const GemmTcKParams& p) {
-        if (p.trace) t0 = clock64();
+        if (TC_TRACE(p)) t0 = clock64();
     }
     __device__ __forceinline__ void stop(const GemmTcKParams& p, int slot) {
-        if (p.trace) atomicAdd(p.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 16 + slot,
+        if (TC_TRACE(p)) atomicAdd(TC_TRACE(p) + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 16 + slot,
                                (unsigned long long)(clock64() - t0));
     }
 };
@@ -489,7 +500,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 if (lane == 0) record_device_error(p.err, kErrGemmTcWait);
             }
             if (!ok) return;
-            if (!(p.dbg & 1)) {
+            if (!(TC_DBG(p) & 1)) {
                 if constexpr (W4)
                     dequant_rows_w4_exact(p, rb, Ws + s * kTcWStage + warp * kW4PairBytes, warp, lane,
                                           Bs + s * kTcTileBytes, scl + (kb % kScl) * kTcBN);
@@ -518,7 +529,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 const float* sc = scl + (kb % kScl) * kTcBN + half * 64;
 #pragma unroll
                 for (int c = 0; c < 2; ++c) {
-                    if (p.dbg & 2) break;
+                    if (TC_DBG(p) & 2) break;
                     uint32_t r[32];
                     tc_ld_32x32b_x32(taddr + (uint32_t)((kb & 1) * kTcBN) + ((uint32_t)(quarter * 32) << 16) +
                                              (uint32_t)(half * 64 + c * 32),
@@ -557,7 +568,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         TcClock cke;
         if (warp == 0 && lane == 0) cke.start(p);
         pdl_wait();
-        if (row < p.m && ok && !(p.dbg & 4)) {
+        if (row < p.m && ok && !(TC_DBG(p) & 4)) {
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 float v[32];
@@ -710,7 +721,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) gemm_w4_swap_kernel(const __gri
                     record_device_error(p.err, kErrGemmTcWait);
                 }
                 if (!ok) break;
-                if (p.dbg & 16) {  // diagnostics: no activation loads
+                if (TC_DBG(p) & 16) {  // diagnostics: no activation loads
                     mbar_arrive(&full[s]);
                     continue;
                 }
@@ -733,7 +744,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) gemm_w4_swap_kernel(const __gri
                     record_device_error(p.err, kErrGemmTcWait);
                 }
                 if (!ok) break;
-                if (p.dbg & 32) {  // diagnostics: no record loads
+                if (TC_DBG(p) & 32) {  // diagnostics: no record loads
                     mbar_arrive(&fullw[s]);
                     continue;
                 }
@@ -816,7 +827,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) gemm_w4_swap_kernel(const __gri
             publish();
             const uint8_t* rec = Ws + sw * kTcWStage + blk * kW4PairBytes;
             uint32_t v[16];
-            if (valid && !(p.dbg & 1)) {
+            if (valid && !(TC_DBG(p) & 1)) {
                 if (pt == 0)
                     scl[(kb % kScl) * kTcBM + r] =
                             __half2float(reinterpret_cast<const __half*>(rec + 1024)[2 * g + hi]);
@@ -863,7 +874,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) gemm_w4_swap_kernel(const __gri
             if (warp == 0 && lane == 0) ck.start(p);
             tc_fence_after();
             const float sc = scl[(kb % kScl) * kTcBM + r];
-            if (!(p.dbg & 2)) {
+            if (!(TC_DBG(p) & 2)) {
                 uint32_t t32[32];
                 tc_ld_32x32b_x32(taddr + lane_base + (uint32_t)((kb & 1) * kTcBN + 32 * pt), t32);
 #pragma unroll
@@ -887,7 +898,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) gemm_w4_swap_kernel(const __gri
         constexpr int OC = SILU ? kTcBM / 2 : kTcBM;  // output columns of the tile
         __nv_bfloat16* T = reinterpret_cast<__nv_bfloat16*>(Xs);
         const int tb = 32 * pt;  // this thread's first token in the tile
-        if (p.dbg & 8) {
+        if (TC_DBG(p) & 8) {
         } else if constexpr (SILU) {
             // rows 0-7 of a 16-row block are gate rows, 8-15 the matching up
             // rows: lanes g and g+8 swap one value per token pair, so each
@@ -906,7 +917,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) gemm_w4_swap_kernel(const __gri
         }
         named_bar_sync(1, kSwDqWarps * 32);
         pdl_wait();
-        if (ok && !(p.dbg & 4)) {
+        if (ok && !(TC_DBG(p) & 4)) {
             const int64_t c0 = SILU ? n0 / 2 : n0;          // first output column of the tile
             const int64_t cend = SILU ? p.n / 2 : p.n;
             constexpr int CH = OC / 8;                      // 16-byte chunks per token row
@@ -975,6 +986,7 @@ bool gemm_tc_supported(const GemmTcParams& p, int fmt) {
 }
 size_t gemm_tc_workspace_bytes(const GemmTcParams&, int) { return 0; }
 
+#ifdef AMCU_DIAG
 static int gemm_dbg() {
     static const int v = [] {
         const char* e = std::getenv("AMCU_GEMM_DBG");
@@ -1009,15 +1021,18 @@ struct TcTrace {
         cudaFree(buf);
     }
 };
+#else
+static int gemm_dbg() { return 0; }
+struct TcTrace {
+    unsigned long long* buf = nullptr;
+    TcTrace(dim3, cudaStream_t) {}
+};
+#endif
 
 template <int FMT, int EPI>
 static am_status_code launch_tc(const GemmTcParams& g, const CUtensorMap& map, cudaStream_t s) {
     auto kern = gemm_tc_kernel<FMT, EPI>;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
-        attr = true;
-    }
+    set_func_attr_once((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes);
     GemmTcKParams p{};
     p.w = static_cast<const uint8_t*>(g.w);
     p.scales = static_cast<const float*>(g.scales);
@@ -1039,11 +1054,7 @@ static am_status_code launch_tc(const GemmTcParams& g, const CUtensorMap& map, c
 template <int EPI>
 static am_status_code launch_swap(const GemmTcParams& g, const CUtensorMap& map, cudaStream_t s) {
     auto kern = gemm_w4_swap_kernel<EPI>;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSwSmemBytes);
-        attr = true;
-    }
+    set_func_attr_once((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSwSmemBytes);
     GemmTcKParams p{};
     p.w = static_cast<const uint8_t*>(g.w);
     p.y = static_cast<__nv_bfloat16*>(g.y);

@@ -360,16 +360,10 @@ __global__ void gemm_plain_kernel(GemvParams p) {
 template <int FMT, int EPI>
 static void launch_gemv_one(GemvParams p, cudaStream_t s) {
     constexpr int kMaxSmem = 200 * 1024;
-    static int smem_per_sm = 0;
-    if (smem_per_sm == 0) {
-        int dev = 0, v = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-        smem_per_sm = v > 0 ? v : 228 * 1024;
-        cudaFuncSetAttribute(gemv_tc_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-    }
+    const int smem_sm = smem_per_sm();
+    set_func_attr_once((const void*)gemv_tc_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
     constexpr int UB = FMT == AMCU_WFMT_INT4 ? kW4PairBytes : 2048;
-    const int per_cta = smem_per_sm / GEMV_CPS - 2048;  // room for the per-CTA reserve
+    const int per_cta = smem_sm / GEMV_CPS - 2048;  // room for the per-CTA reserve
     int su = stage_units<FMT>(p.k);
     // long rows (one activation row of K above ~24K columns): the large stages
     // would leave room for one CTA per SM, so they go back to 16 records
@@ -381,7 +375,7 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
     while (stages > 2 && gemv_smem<FMT>(1, p.k, sby, stages).total > per_cta) --stages;
     p.stages = stages;
     p.stage_units = su;
-    int per_sm = smem_per_sm / (gemv_smem<FMT>(1, p.k, sby, stages).total + 1024);
+    int per_sm = smem_sm / (gemv_smem<FMT>(1, p.k, sby, stages).total + 1024);
 #ifdef GEMV_GRID_CPS
     // size the grid for fewer CTAs per SM than fit, leaving room for the next
     // kernel's CTAs to start (and stream their weights) early

@@ -177,12 +177,12 @@ Status KVCacheManager::Init(CudaAllocator& alloc, size_t L, size_t H, size_t T, 
 }
 
 StatusOr<KVCacheView> KVCacheManager::ReserveForSession(size_t prompt_len, size_t max_new) {
-    if (!initialized_) return Status::FailedPrecondition("KVCacheManager is not initialized");
-    if (slot_.in_use) return Status::FailedPrecondition("KVCacheManager already has an active session reservation");
+    if (!initialized_) return Status::FailedPrecondition("the KV cache has not been set up (call Init first)");
+    if (slot_.in_use) return Status::FailedPrecondition("a session already holds the KV cache; release it before reserving again");
     const size_t req = prompt_len + max_new;
-    if (req < prompt_len) return Status::Overflow("KV session reservation overflowed size_t");
-    if (req == 0) return Status::InvalidArgument("KV session reservation must request at least one token");
-    if (req > layout_.max_tokens) return Status::OutOfRange("KV session reservation exceeds physical KV capacity");
+    if (req < prompt_len) return Status::Overflow("prompt_len + max_new does not fit in size_t");
+    if (req == 0) return Status::InvalidArgument("a KV reservation needs prompt_len + max_new >= 1");
+    if (req > layout_.max_tokens) return Status::OutOfRange("prompt_len + max_new is larger than the KV cache's max_tokens");
     ++slot_.generation;
     slot_.in_use = true;
     slot_.capacity_tokens = req;
@@ -192,15 +192,15 @@ StatusOr<KVCacheView> KVCacheManager::ReserveForSession(size_t prompt_len, size_
 }
 
 Status KVCacheManager::ResetSession(KVCacheView& view) {
-    if (!initialized_) return Status::FailedPrecondition("KVCacheManager is not initialized");
-    if (!view.valid()) return Status::FailedPrecondition("Cannot reset an invalid or stale KVCacheView");
+    if (!initialized_) return Status::FailedPrecondition("the KV cache has not been set up (call Init first)");
+    if (!view.valid()) return Status::FailedPrecondition("this KV view was released or belongs to an older reservation (reset)");
     slot_.current_pos = slot_.prompt_len;
     return Status::Ok();
 }
 
 Status KVCacheManager::ReleaseSession(KVCacheView& view) {
-    if (!initialized_) return Status::FailedPrecondition("KVCacheManager is not initialized");
-    if (!view.valid()) return Status::FailedPrecondition("Cannot release an invalid or stale KVCacheView");
+    if (!initialized_) return Status::FailedPrecondition("the KV cache has not been set up (call Init first)");
+    if (!view.valid()) return Status::FailedPrecondition("this KV view was released or belongs to an older reservation (release)");
     slot_.in_use = false;
     slot_.capacity_tokens = slot_.prompt_len = slot_.current_pos = 0;
     ++slot_.generation;
@@ -373,6 +373,7 @@ Status Communicator::AllReduceAddBf16(const void* part, void* x, int64_t n, cuda
     p.world = world_;
     for (int r = 0; r < world_; ++r) p.area[r] = static_cast<uint8_t*>(peers_[r]);
     p.err = amcu::device_error_word();
+    p.wait_ns = wait_ns_;
     amcu::launch_ar_oneshot_add(p, s);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? Status::Ok() : Status::Internal(std::string("one-shot all-reduce: ") + cudaGetErrorString(e));

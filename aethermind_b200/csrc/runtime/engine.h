@@ -201,6 +201,8 @@ public:
     Status OpenPeers(const void* handles);  // world x 64 bytes, rank order
     bool OneShotReady(int64_t n) const;
     Status AllReduceAddBf16(const void* part, void* x, int64_t n, cudaStream_t s);
+    // Bound of the one-shot all-reduce's wait for the peers (0: about 2 s).
+    void set_wait_ns(uint64_t ns) { wait_ns_ = ns; }
 
 private:
     void* comm_ = nullptr;
@@ -208,6 +210,7 @@ private:
     void* area_ = nullptr;          // this rank's exchange area
     void* peers_[8] = {};           // every rank's area as mapped here
     bool peers_open_ = false;
+    uint64_t wait_ns_ = 0;
 };
 Status NcclGetUniqueId(void* out128);
 

@@ -24,6 +24,7 @@
 
 #include <nvtx3/nvToolsExt.h>
 
+#include "amcu_internal.h"
 #include "kernels/decode_state.cuh"
 #include "runtime/engine.h"
 
@@ -774,8 +775,26 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
     int32_t status_h = 0;
     int32_t* hstatus = reinterpret_cast<int32_t*>(hg + c.max_batch * s->out_cap);
     AM_CUDA(cudaMemcpyAsync(hstatus, s->status.data(), 4, cudaMemcpyDeviceToHost, st));
+    // The device error word collects the codes of bounded waits that ran out
+    // (a tensor-parallel peer that never arrived, a stalled copy): the kernel
+    // that gave up skipped its wait, so the tokens of this call cannot be
+    // trusted. Read it with the results and clear it for the next call.
+    int32_t* dev_err = amcu::device_error_word();
+    if (!dev_err) return Status::Internal("device error word unavailable");
+    hstatus[1] = 0;
+    AM_CUDA(cudaMemcpyAsync(hstatus + 1, dev_err, 4, cudaMemcpyDeviceToHost, st));
     AM_CUDA(cudaStreamSynchronize(st));
-    status_h = *hstatus;
+    status_h = hstatus[0];
+    if (hstatus[1] != 0) {
+        const int32_t code = hstatus[1];
+        AM_CUDA(cudaMemsetAsync(dev_err, 0, 4, st));
+        AM_CUDA(cudaStreamSynchronize(st));
+        char msg[160];
+        std::snprintf(msg, sizeof msg,
+                      "a kernel's bounded wait ran out (device error code 0x%x); the generated tokens are invalid",
+                      (unsigned)code);
+        return Status::DeadlineExceeded(msg);
+    }
     if (status_h != 0) return Status(static_cast<StatusCode>(status_h), "device reported an out-of-range index");
     AM_RETURN_IF_ERROR(kv.CommitUntil(P + N - 1));
     out.resize(B * N);

@@ -402,6 +402,30 @@ typedef struct AmcuEmbeddingArgs {
 am_status_code amcu_embedding(const AmcuEmbeddingArgs* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* One-shot all-reduce + residual add over peer memory (tensor-parallel      */
+/* decode): x = round(x + round(sum over ranks of part_r)), bf16, n elements. */
+/* Replaces the per-block NCCL all-reduce that tensor-parallel row splits     */
+/* need after o_proj / down_proj; the reference engine runs on one device and */
+/* has no collective (its LayerRunner, src/execution/layer_runner.cpp:24-93, */
+/* would call it after those Linears).                                        */
+/* areas[r]: rank r's exchange area as mapped in this process (own area       */
+/* included; peers' through CUDA IPC), each amcu_allreduce_area_bytes()       */
+/* bytes, zeroed before first use. The wait for the peers is bounded by       */
+/* wait_limit_us (0: about 2 s); when it runs out the kernel records 0x401 in */
+/* the device error word (amcu_device_error) and returns instead of hanging.  */
+/* ------------------------------------------------------------------------ */
+typedef struct AmcuAllReduceArgs {
+    const void* part;      /* this rank's bf16 partial [n] */
+    void* x;               /* bf16 residual [n], updated in place */
+    int64_t n;             /* multiple of 8, at most 65536 */
+    int32_t rank, world;   /* world in [2, 8] */
+    void* areas[8];
+    uint64_t wait_limit_us;
+} AmcuAllReduceArgs;
+size_t amcu_allreduce_area_bytes(void);
+am_status_code amcu_allreduce_oneshot_add(const AmcuAllReduceArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Session API (reference product spec: docs/products/aethermind_prd.md:     */
 /* 296-320; the reference has not implemented it).                          */
 /* ------------------------------------------------------------------------ */

@@ -9,6 +9,10 @@ from __future__ import annotations
 
 import numpy as np
 
+# Near-tie threshold for bf16 models (logits stored in bf16, 0.03125 apart in
+# [4, 8)): 4 bf16 ulps there.
+NEAR_TIE_BF16 = 0.125
+
 
 def tiny_weights(cfg, seed: int = 0) -> dict[str, np.ndarray]:
     rng = np.random.default_rng(seed)
@@ -53,3 +57,24 @@ def load_tiny_into_engine(model, w):
     # dict order sets every layer's "wg" before its "wu" (the fused gate/up pack needs both)
     for name, arr in w.items():
         model.set_weight(name, arr)
+
+
+def walk_greedy(sess, prompt, ref, gaps, near_tie):
+    """Compares the engine with the oracle's greedy sequence `ref` at every
+    position; returns the positions where a near-tie flipped the token."""
+    flips = []
+    start = 0
+    while start < len(ref):
+        pre = np.concatenate([prompt, ref[:start].astype(np.uint32)])
+        got = sess.generate(pre, len(ref) - start)
+        for j, (a, b) in enumerate(zip(got.tolist(), ref[start:].tolist())):
+            i = start + j
+            if a != b:
+                assert gaps[i] < near_tie, (f"position {i}: engine {a} != oracle {b} with oracle gap "
+                                            f"{gaps[i]:.4g} >= {near_tie}")
+                flips.append(i)
+                start = i + 1
+                break
+        else:
+            start = len(ref)
+    return flips

@@ -224,6 +224,55 @@ def test_prefill_gemm_matches_torch_fp32(ops, orc, fmt, m):
 
 
 @pytest.mark.parametrize("fmt", ["int4", "int8"])
+@pytest.mark.parametrize("m", [64, 512])
+def test_prefill_gemm_n14336_matches_oracle(ops, orc, fmt, m):
+    """The op sweep's N = 14336 (K = 4096) through the tensor-core GEMM at
+    m = 64 and 512, against the CPU oracle's Linear."""
+    n, k = 14336, 4096
+    pw, host = _w(ops, orc, fmt, n, k, seed=31)
+    x = orc.bf16_round(np.random.default_rng(m + 7).normal(0, 1, (m, k)).astype(np.float32))
+    entry = "amcu_gemm_w4g128_prefill" if fmt == "int4" else "amcu_gemm_w8_prefill"
+    y = ops.linear(bf16_dev(x), pw, entry=entry)
+    np.testing.assert_allclose(to_np(y), _oracle_linear(orc, fmt, x, host), rtol=BF_RTOL, atol=BF_ATOL)
+
+
+def _one_hot_expected(fmt, host, n, cols):
+    """bf16(q[n, k] * s) for the columns k in `cols`: rows [len(cols), n]."""
+    from oracle import bf16_round, unpack_w4
+    if fmt == "int4":
+        q = unpack_w4(host[0], n, len(host[0][0]) * 2).astype(np.float32)
+        s = host[1].view(np.float16).astype(np.float32)
+        return bf16_round(np.stack([q[:, c] * s[:, c // 128] for c in cols]) + np.float32(0))  # -0 -> +0
+    q = host[0].astype(np.float32)
+    return bf16_round(np.stack([q[:, c] * host[1] for c in cols]) + np.float32(0))
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
+@pytest.mark.parametrize("entry_kind,m", [("gemv", 1), ("gemv", 8), ("gemm", 64), ("gemm", 512)])
+def test_in_kernel_dequant_bit_exact(ops, orc, fmt, entry_kind, m):
+    """One-hot activation rows pick single weight columns: the output must be
+    bf16(q[n, k] * s[n, group]) (INT4) or bf16(q[n, k] * s[n]) (INT8) bit for
+    bit, which pins the kernels' nibble/byte unpacking, the group and scale
+    indexing and the offset removal (no rounding happens before the final
+    bf16 store: q * s is exact in fp32 for INT4, one fp32 rounding for INT8,
+    as in the reference's dequant). Every column of K is covered."""
+    n, k = 256, 1024
+    pw, host = _w(ops, orc, fmt, n, k, seed=41)
+    entry = {("gemv", "int4"): "amcu_gemv_w4g128", ("gemv", "int8"): "amcu_gemv_w8",
+             ("gemm", "int4"): "amcu_gemm_w4g128_prefill", ("gemm", "int8"): "amcu_gemm_w8_prefill"}[
+        (entry_kind, fmt)]
+    order = np.random.default_rng(m).permutation(k)
+    for c0 in range(0, k, m):
+        cols = order[c0:c0 + m]
+        x = np.zeros((len(cols), k), np.float32)
+        x[np.arange(len(cols)), cols] = 1.0
+        y = ops.linear(bf16_dev(x), pw, entry=entry)
+        got = y.cpu().view(torch.int16).numpy().view(np.uint16)
+        want = orc.f32_to_bf16_bits(_one_hot_expected(fmt, host, n, cols))
+        np.testing.assert_array_equal(got, want, err_msg=f"columns {cols[:8]}...")
+
+
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
 def test_prefill_gemm_epilogues_ragged_tiles(ops, orc, fmt):
     """Tensor-core GEMM with m and n that do not fill the 128 x 128 tiles:
     residual add (in place) and the gate/up SiLU-Mul epilogue against the

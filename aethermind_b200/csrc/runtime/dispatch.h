@@ -49,9 +49,12 @@ enum class OpType : uint16_t {
 };
 const char* ToString(OpType op) noexcept;
 
-enum class DeviceType : int32_t { kUndefined = 0, kCPU = 1, kCUDA = 2 };
+// Same type and values as the reference's DeviceType (include/aethermind/base/device.h:23-28).
+enum class DeviceType : uint8_t { kCPU = 0, kCUDA, kCANN, kUndefined };
 
-// The element types used on the path (a subset of the reference DataType).
+// The element types used on the path. The reference's DataType is a DLPack-style
+// (code, bits, lanes) triple; this engine only needs these, and the reference
+// plugin (reference_plugin/cuda_backend_plugin.cpp) converts at the boundary.
 enum class DType : uint8_t { kUndefined = 0, kF32, kBF16, kF16, kI8, kI4, kI32, kI64, kU32 };
 
 enum class IsaLevel : uint8_t { kScalar = 0, kAVX2, kAVX512, kAMX };

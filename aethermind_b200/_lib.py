@@ -96,6 +96,11 @@ class AmModelConfig(C.Structure):
                 ("max_seq", C.c_int64), ("max_batch", C.c_int64)]
 
 
+class AmLoadOptions(C.Structure):
+    _fields_ = [("weight_format", C.c_int32), ("act_dtype", C.c_int32), ("max_seq", C.c_int64),
+                ("max_batch", C.c_int64)]
+
+
 class AmSessionConfig(C.Structure):
     _fields_ = [("max_new_tokens", C.c_int64), ("use_cuda_graph", C.c_int32), ("unfused_attention", C.c_int32),
                 ("persistent_decode", C.c_int32)]
@@ -156,6 +161,9 @@ _SIGS = {
     "am_runtime_open_peers": (C.c_int, [P, P]),
     "am_last_error": (C.c_char_p, []),
     "am_model_load": (P, [P, C.c_char_p, C.POINTER(P)]),
+    "am_model_load_ex": (P, [P, C.c_char_p, C.POINTER(AmLoadOptions), C.POINTER(P)]),
+    "amcu_quantize_weight": (C.c_int, [C.c_int32, P, C.c_int32, C.c_int64, C.c_int64, C.c_int64, P, P, P]),
+    "amcu_convert": (C.c_int, [P, C.c_int32, P, C.c_int32, C.c_int64, P]),
     "am_model_create": (P, [P, C.POINTER(AmModelConfig), C.POINTER(P)]),
     "am_model_init_synthetic": (C.c_int, [P, C.c_uint64]),
     "am_model_set_weight": (C.c_int, [P, C.c_char_p, P, P]),

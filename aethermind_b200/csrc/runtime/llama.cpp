@@ -27,6 +27,7 @@
 #include "amcu_internal.h"
 #include "kernels/decode_state.cuh"
 #include "runtime/engine.h"
+#include "runtime/hf_checkpoint.h"
 
 namespace aethermind {
 namespace {
@@ -492,13 +493,13 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
                                   {ids, table}, {MView2(s->x.data(), A, M, H, H)}, &ea, nullptr, "embedding"));
     }
     RmsNormAttrs na{c.rms_eps};
-    // Decode of a bs <= 2 INT4 model on one GPU: every decoder layer in one
+    // Decode of a batch-1 INT4 model on one GPU: every decoder layer in one
     // persistent launch (amcu_decode_stack), when the session asks for it.
     const KernelSelector stack_sel = pb.Sel(A, DType::kI4, WeightFormat::kQuantizedInt4);
-    const bool use_stack = phase == ExecPhase::kDecode && R == 1 && B <= 2 && !tp &&
+    const bool use_stack = phase == ExecPhase::kDecode && R == 1 && B == 1 && !tp &&
                            wf == WeightFormat::kQuantizedInt4 && A == DType::kBF16 &&
-                           s->cfg.persistent_decode != 0 && c.hidden % 2048 == 0 && m->inter_l % 2048 == 0 &&
-                           (m->nq_l * d) % 2048 == 0 && m->rt->backend->ResolveKernelInfo(OpType::kDecodeStack, stack_sel).ok();
+                           s->cfg.persistent_decode != 0 && c.hidden <= 16384 && m->inter_l <= 16384 &&
+                           m->nq_l * d <= 16384 && m->rt->backend->ResolveKernelInfo(OpType::kDecodeStack, stack_sel).ok();
     if (use_stack) {
         std::vector<AmcuDecodeLayer> tab(c.layers);
         for (int64_t l = 0; l < c.layers; ++l) {
@@ -815,6 +816,138 @@ Status Generate(am_session_s* s, const uint32_t* in, int64_t B, int64_t P, int64
     return Status::Ok();
 }
 
+// ---- checkpoint loading (am_model_load) ----
+
+int32_t AmcuDtypeOf(hf::TensorDtype t) {
+    return t == hf::TensorDtype::kF32 ? AMCU_F32 : t == hf::TensorDtype::kBF16 ? AMCU_BF16 : AMCU_F16;
+}
+
+Status CheckShape(const std::string& name, const hf::TensorInfo& t, std::vector<int64_t> want) {
+    if (t.shape != want) {
+        std::string got, exp;
+        for (int64_t d : t.shape) got += std::to_string(d) + ",";
+        for (int64_t d : want) exp += std::to_string(d) + ",";
+        return Status::InvalidArgument("tensor '" + name + "' has shape [" + got + "], expected [" + exp + "]");
+    }
+    return Status::Ok();
+}
+
+// The raw checkpoint tensor on the device (its own dtype).
+Status UploadRaw(am_model_s* m, const hf::TensorInfo& t, DeviceBuffer& out) {
+    AM_RETURN_IF_ERROR(AllocVec(m, out, t.bytes));
+    return CudaOk(UploadSync(m, out.data(), t.data, t.bytes), "checkpoint upload");
+}
+
+// A raw [n][k] tensor -> a canonical device matrix of the model's format:
+// quantized (INT4 / INT8) or converted to the activation dtype (plain).
+Status CanonFromRaw(am_model_s* m, const hf::TensorInfo& t, const DeviceBuffer& raw, int64_t n, int64_t k, Canon& out) {
+    const auto& c = m->cfg;
+    cudaStream_t st = m->rt->stream;
+    out.n = n;
+    out.k = k;
+    AM_RETURN_IF_ERROR(AllocVec(m, out.q, RowBytes(c, k) * n));
+    if (c.weight_format == AMCU_WFMT_PLAIN) {
+        AM_RETURN_IF_ERROR(Status::FromAm(amcu_convert(raw.data(), AmcuDtypeOf(t.dtype), out.q.data(), c.act_dtype,
+                                                       n * k, st),
+                                          amcu_last_error()));
+    } else {
+        AM_RETURN_IF_ERROR(AllocVec(m, out.s, ScaleRowBytes(c, k) * n));
+        AM_RETURN_IF_ERROR(Status::FromAm(amcu_quantize_weight(c.weight_format, raw.data(), AmcuDtypeOf(t.dtype), n, k,
+                                                               c.group_size, out.q.data(), out.s.data(), st),
+                                          amcu_last_error()));
+    }
+    return CudaOk(cudaStreamSynchronize(st), "quantize");
+}
+
+Status ConvertInto(am_model_s* m, const hf::TensorInfo& t, DeviceBuffer& dst, int64_t count) {
+    DeviceBuffer raw;
+    AM_RETURN_IF_ERROR(UploadRaw(m, t, raw));
+    AM_RETURN_IF_ERROR(Status::FromAm(amcu_convert(raw.data(), AmcuDtypeOf(t.dtype), dst.data(), m->cfg.act_dtype,
+                                                   count, m->rt->stream),
+                                      amcu_last_error()));
+    return CudaOk(cudaStreamSynchronize(m->rt->stream), "convert");
+}
+
+// Every tensor of the checkpoint into the model (names as the reference's
+// HF weight resolver reads them, src/model/formats/hf/hf_weight_resolver.cpp).
+Status LoadCheckpoint(am_model_s* m, const hf::Checkpoint& ck, bool tied_in_file) {
+    const auto& c = m->cfg;
+    const int64_t H = c.hidden, d = c.head_dim;
+    auto get = [&](const std::string& name, std::vector<int64_t> shape) -> StatusOr<const hf::TensorInfo*> {
+        auto t = ck.Get(name);
+        if (!t.ok()) return t.status();
+        AM_RETURN_IF_ERROR(CheckShape(name, *t.value(), std::move(shape)));
+        return t.value();
+    };
+    // embedding (and the tied lm_head)
+    {
+        auto e = get("model.embed_tokens.weight", {c.vocab, H});
+        if (!e.ok()) return e.status();
+        const hf::TensorInfo& et = *e.value();
+        DeviceBuffer raw;
+        AM_RETURN_IF_ERROR(UploadRaw(m, et, raw));
+        if (c.tied_embeddings && c.weight_format == AMCU_WFMT_INT8) {
+            // one INT8 matrix serves both: dequantized rows for the embedding
+            Canon full;
+            AM_RETURN_IF_ERROR(CanonFromRaw(m, et, raw, c.vocab, H, full));
+            AM_CUDA(cudaMemcpyAsync(m->embed.data(), full.q.data(), c.vocab * H, cudaMemcpyDeviceToDevice, m->rt->stream));
+            AM_CUDA(cudaMemcpyAsync(m->embed_scales.data(), full.s.data(), c.vocab * 4, cudaMemcpyDeviceToDevice,
+                                    m->rt->stream));
+            AM_RETURN_IF_ERROR(PackInto(m, m->lm_head, 0, full));
+        } else {
+            AM_RETURN_IF_ERROR(Status::FromAm(amcu_convert(raw.data(), AmcuDtypeOf(et.dtype), m->embed.data(), c.act_dtype,
+                                                           c.vocab * H, m->rt->stream),
+                                              amcu_last_error()));
+            AM_CUDA(cudaStreamSynchronize(m->rt->stream));
+            if (tied_in_file) {  // plain tied, or an INT4 model that keeps its own quantized lm_head copy
+                Canon head;
+                AM_RETURN_IF_ERROR(CanonFromRaw(m, et, raw, c.vocab, H, head));
+                AM_RETURN_IF_ERROR(PackInto(m, m->lm_head, 0, head));
+            }
+        }
+    }
+    if (!tied_in_file) {
+        auto h = get("lm_head.weight", {c.vocab, H});
+        if (!h.ok()) return h.status();
+        DeviceBuffer raw;
+        AM_RETURN_IF_ERROR(UploadRaw(m, *h.value(), raw));
+        Canon head;
+        AM_RETURN_IF_ERROR(CanonFromRaw(m, *h.value(), raw, c.vocab, H, head));
+        AM_RETURN_IF_ERROR(PackInto(m, m->lm_head, 0, head));
+    }
+    {
+        auto fnorm = get("model.norm.weight", {H});
+        if (!fnorm.ok()) return fnorm.status();
+        AM_RETURN_IF_ERROR(ConvertInto(m, *fnorm.value(), m->final_norm, H));
+    }
+    const char* hf_names[7] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                               "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"};
+    const char* names[7] = {"wq", "wk", "wv", "wo", "wg", "wu", "wd"};
+    for (int64_t l = 0; l < c.layers; ++l) {
+        const std::string pre = "model.layers." + std::to_string(l) + ".";
+        auto in = get(pre + "input_layernorm.weight", {H});
+        if (!in.ok()) return in.status();
+        AM_RETURN_IF_ERROR(ConvertInto(m, *in.value(), m->layers[l].attn_norm, H));
+        auto post = get(pre + "post_attention_layernorm.weight", {H});
+        if (!post.ok()) return post.status();
+        AM_RETURN_IF_ERROR(ConvertInto(m, *post.value(), m->layers[l].mlp_norm, H));
+        for (int t = 0; t < 7; ++t) {
+            Target tg;
+            AM_RETURN_IF_ERROR(ResolveTarget(m, (int)l, names[t], tg));
+            auto w = get(pre + hf_names[t] + ".weight", {tg.n_full, tg.k_full});
+            if (!w.ok()) return w.status();
+            DeviceBuffer raw;
+            AM_RETURN_IF_ERROR(UploadRaw(m, *w.value(), raw));
+            Canon full, shard;
+            AM_RETURN_IF_ERROR(CanonFromRaw(m, *w.value(), raw, tg.n_full, tg.k_full, full));
+            AM_RETURN_IF_ERROR(Shard(m, full, tg.split, 0, shard));
+            AM_RETURN_IF_ERROR(StoreLinear(m, (int)l, tg, shard));
+        }
+        (void)d;
+    }
+    return CudaOk(cudaDeviceSynchronize(), "checkpoint load");
+}
+
 }  // namespace
 }  // namespace aethermind
 
@@ -874,15 +1007,6 @@ am_status_code am_nccl_get_unique_id(void* out128) {
 }
 
 const char* am_last_error(void) { return g_err.c_str(); }
-
-am_model_t am_model_load(am_runtime_t, const char* path, am_error_t* error) {
-    if (error)
-        *error = am_error_create(AM_STATUS_UNIMPLEMENTED,
-                                 (std::string("am_model_load: checkpoint loading is not implemented (") +
-                                  (path ? path : "") + ")")
-                                         .c_str());
-    return nullptr;
-}
 
 am_model_t am_model_create(am_runtime_t rt, const am_model_config_t* cfg, am_error_t* error) {
     auto fail = [&](const Status& s) -> am_model_t {
@@ -950,6 +1074,62 @@ am_model_t am_model_create(am_runtime_t rt, const am_model_config_t* cfg, am_err
         return fail(s);
     }
     return m;
+}
+
+am_model_t am_model_load_ex(am_runtime_t rt, const char* path, const am_load_options_t* opt, am_error_t* error) {
+    auto fail = [&](const Status& s) -> am_model_t {
+        g_err = s.ToString();
+        if (error) *error = am_error_create(s.am_code(), s.message().c_str());
+        return nullptr;
+    };
+    if (!rt || !path) return fail(Status::InvalidArgument("am_model_load: null runtime or path"));
+    auto ck = hf::Checkpoint::Open(path);
+    if (!ck.ok()) return fail(ck.status());
+    const hf::LlamaConfig& hc = ck.value()->config();
+    am_load_options_t o{};
+    if (opt) o = *opt;
+    am_model_config_t mc{};
+    mc.vocab = hc.vocab;
+    mc.hidden = hc.hidden;
+    mc.layers = hc.layers;
+    mc.n_q_heads = hc.n_q_heads;
+    mc.n_kv_heads = hc.n_kv_heads;
+    mc.head_dim = hc.head_dim;
+    mc.inter = hc.inter;
+    mc.rms_eps = hc.rms_eps;
+    mc.rope_theta = hc.rope_theta;
+    mc.weight_format = o.weight_format ? o.weight_format : AMCU_WFMT_INT4;
+    mc.act_dtype = o.act_dtype ? o.act_dtype : AMCU_BF16;
+    mc.group_size = 128;
+    mc.max_seq = o.max_seq > 0 ? o.max_seq : (hc.max_position_embeddings < 4096 ? hc.max_position_embeddings : 4096);
+    mc.max_batch = o.max_batch > 0 ? o.max_batch : 1;
+    // a checkpoint without lm_head.weight ties it to the embedding
+    const bool tied_in_file = hc.tied_embeddings || !ck.value()->Has("lm_head.weight");
+    // INT4 keeps a quantized copy of a tied lm_head next to the bf16 embedding
+    mc.tied_embeddings = tied_in_file && mc.weight_format != AMCU_WFMT_INT4;
+    am_error_t cerr = nullptr;
+    am_model_t m = am_model_create(rt, &mc, &cerr);
+    if (!m) {
+        Status s(static_cast<StatusCode>(cerr ? am_error_code(cerr) : AM_STATUS_INTERNAL),
+                 std::string("am_model_load: ") + (cerr ? am_error_message(cerr) : "model create failed"));
+        if (cerr) am_error_destroy(cerr);
+        return fail(s);
+    }
+    Status st;
+    try {
+        st = LoadCheckpoint(m, *ck.value(), tied_in_file);
+    } catch (const Status& s) {
+        st = s;
+    }
+    if (!st.ok()) {
+        am_model_unload(m);
+        return fail(st);
+    }
+    return m;
+}
+
+am_model_t am_model_load(am_runtime_t rt, const char* path, am_error_t* error) {
+    return am_model_load_ex(rt, path, nullptr, error);
 }
 
 void am_model_unload(am_model_t m) { delete m; }

@@ -113,6 +113,25 @@ class Model:
             raise AmError(code, f"am_model_create: {msg}")
         self.h = h
 
+    @classmethod
+    def load(cls, rt: Runtime, path: str, weight_format: int = L.WFMT_INT4, act_dtype: int = L.BF16,
+             max_seq: int = 0, max_batch: int = 0) -> "Model":
+        """A model from a Hugging Face Llama checkpoint directory (config.json +
+        safetensors), quantized on the device at load time (am_model_load_ex)."""
+        o = L.AmLoadOptions()
+        o.weight_format, o.act_dtype, o.max_seq, o.max_batch = weight_format, act_dtype, max_seq, max_batch
+        err = C.c_void_p()
+        h = lib().am_model_load_ex(rt.h, str(path).encode(), C.byref(o), C.byref(err))
+        if not h:
+            code = lib().am_error_code(err) if err.value else 13
+            msg = lib().am_error_message(err).decode() if err.value else ""
+            if err.value:
+                lib().am_error_destroy(err)
+            raise AmError(code, f"am_model_load: {msg}")
+        self = cls.__new__(cls)
+        self.rt, self.cfg, self._c, self.h = rt, None, None, h
+        return self
+
     def init_synthetic(self, seed: int = 0) -> None:
         L.check(lib().am_model_init_synthetic(self.h, seed), "am_model_init_synthetic")
 

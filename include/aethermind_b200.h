@@ -300,9 +300,10 @@ am_status_code amcu_attn_decode(const AmcuAttentionArgs* args, void* stream);
 /* every decoder layer of BuildLlamaDense -- attention RMSNorm, q/k/v        */
 /* Linear, RoPE, KVCacheUpdate, Attention, o Linear + Add, MLP RMSNorm,      */
 /* gate/up Linear + SiluMul, down Linear + Add -- for one decode step of a   */
-/* bs <= 2, INT4 g128, bf16 model in one cooperative launch; one CTA per SM   */
+/* batch-1, INT4 g128, bf16 model in one cooperative launch; one CTA per SM   */
 /* streams its share of every layer's weights without pausing at the layer   */
-/* or phase boundaries).                                                      */
+/* or phase boundaries). hidden, inter and n_q*head_dim: multiples of 128,   */
+/* at most 16384.                                                             */
 /* ------------------------------------------------------------------------ */
 typedef struct AmcuDecodeLayer {   /* one decoder layer, device pointers */
     const void* w_qkv;             /* INT4 [(nq + 2 nkv) * head_dim][hidden], device format */
@@ -317,11 +318,11 @@ typedef struct AmcuDecodeLayer {   /* one decoder layer, device pointers */
 typedef struct AmcuDecodeStackArgs {
     const AmcuDecodeLayer* layers; /* device array of n_layers descriptors */
     int64_t n_layers;
-    int64_t batch;                 /* sequences (one row each), 1 or 2 */
+    int64_t batch;                 /* sequences: 1 */
     int64_t hidden, inter, n_q_heads, n_kv_heads, head_dim;
     void* x;                       /* [batch][hidden] bf16 residual stream, updated in place */
     void* qkv;                     /* [batch][(nq + 2 nkv) * head_dim] bf16 scratch */
-    void* attn;                    /* [batch][nq * head_dim] bf16 scratch */
+    void* attn;                    /* unused (the attention output is merged inside the step) */
     void* act;                     /* [batch][inter] bf16 scratch */
     const int32_t* seq_pos;        /* [batch] position of each sequence's token */
     int64_t capacity, slot_stride; /* KV cache (slot_stride 0: n_kv * capacity * head_dim) */
@@ -402,6 +403,22 @@ typedef struct AmcuEmbeddingArgs {
 am_status_code amcu_embedding(const AmcuEmbeddingArgs* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Offline weight quantizer and dtype conversion (checkpoint loading). The    */
+/* reference declares INT8 per-channel / INT4 group-wise weight-only formats */
+/* (docs/products/aethermind_prd.md:216; QuantizationSpec,                    */
+/* include/aethermind/graph/graph_types.h:123-138) but has no quantizer.      */
+/* Symmetric absmax, written in the canonical formats above:                  */
+/*   INT4: s = fp16(max|w| / 7) per (row, group of 128), q = clamp(rint(w/s), */
+/*         -8, 7); INT8: s = max|w| / 127 per row, q = clamp(rint(w/s), ±127). */
+/* w: device [n][k] in AMCU_F32 / AMCU_BF16 / AMCU_F16.                       */
+/* ------------------------------------------------------------------------ */
+am_status_code amcu_quantize_weight(int32_t format, const void* w, int32_t w_dtype, int64_t n, int64_t k,
+                                    int64_t group, void* q, void* scales, void* stream);
+/* dst[i] = src[i] converted (f32 / bf16 / f16 -> f32 / bf16, round to nearest even). */
+am_status_code amcu_convert(const void* src, int32_t src_dtype, void* dst, int32_t dst_dtype, int64_t count,
+                            void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* One-shot all-reduce + residual add over peer memory (tensor-parallel      */
 /* decode): x = round(x + round(sum over ranks of part_r)), bf16, n elements. */
 /* Replaces the per-block NCCL all-reduce that tensor-parallel row splits     */
@@ -465,9 +482,23 @@ typedef struct am_session_config_t {
 am_runtime_t am_runtime_create(const am_config_t* config);
 void am_runtime_destroy(am_runtime_t runtime);
 
-/* Weights from an on-disk checkpoint. Not supported yet: returns NULL with
- * AM_STATUS_UNIMPLEMENTED (synthetic and host-provided weights only). */
+/* Weights from a Hugging Face Llama checkpoint directory (the reference's
+ * ModelLoader::Load, src/model/model_loader.cpp:12-55): config.json plus
+ * model.safetensors or model.safetensors.index.json and its shards; F32, BF16
+ * or F16 tensors, quantized on the device at load time. am_model_load uses the
+ * default options: INT4 g128 weights, bf16 activations, max_seq =
+ * min(max_position_embeddings, 4096), max_batch 1. Errors: NOT_FOUND for a
+ * missing directory or file, INVALID_ARGUMENT for a malformed config, header,
+ * missing tensor or shape mismatch, UNIMPLEMENTED for rope scaling. */
+typedef struct am_load_options_t {
+    int32_t weight_format;   /* AMCU_WFMT_INT4 (0 = default), AMCU_WFMT_INT8 or AMCU_WFMT_PLAIN */
+    int32_t act_dtype;       /* AMCU_BF16 (default) or AMCU_F32 (plain weights only) */
+    int64_t max_seq;         /* 0: min(max_position_embeddings, 4096) */
+    int64_t max_batch;       /* 0: 1 */
+} am_load_options_t;
 am_model_t am_model_load(am_runtime_t runtime, const char* path, am_error_t* error);
+am_model_t am_model_load_ex(am_runtime_t runtime, const char* path, const am_load_options_t* options,
+                            am_error_t* error);
 /* Creates a model with device storage for every weight (uninitialised). */
 am_model_t am_model_create(am_runtime_t runtime, const am_model_config_t* config, am_error_t* error);
 /* Fills every weight from the seeded synthetic generator on the device. */

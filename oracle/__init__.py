@@ -169,6 +169,33 @@ def pack_w4(q: np.ndarray) -> np.ndarray:
     return out
 
 
+def quantize_w4(w: np.ndarray, group: int = 128):
+    """Symmetric absmax INT4 quantization per (row, group of 128) -- the
+    recipe of the engine's checkpoint quantizer (amcu_quantize_weight):
+    s = fp16(max|w| / 7), q = clip(rint(w / s), -8, 7), all in fp32 with
+    correctly rounded division; returns (packed [n][k/2] uint8, s fp16 bits)."""
+    w = np.ascontiguousarray(w, np.float32)
+    n, k = w.shape
+    g = w.reshape(n, k // group, group)
+    s16 = (np.abs(g).max(-1) / np.float32(7)).astype(np.float16)
+    sc = s16.astype(np.float32)[..., None]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(sc > 0, np.rint(g / np.where(sc > 0, sc, np.float32(1))), np.float32(0))
+    q = np.clip(q, -8, 7).astype(np.int8).reshape(n, k)
+    return pack_w4(q), s16.view(np.uint16)
+
+
+def quantize_w8(w: np.ndarray):
+    """Symmetric absmax INT8 per output row: s = max|w| / 127 (fp32),
+    q = clip(rint(w / s), -127, 127); returns (q int8 [n][k], s fp32 [n])."""
+    w = np.ascontiguousarray(w, np.float32)
+    s = (np.abs(w).max(-1) / np.float32(127)).astype(np.float32)
+    sc = s[:, None]
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(sc > 0, np.rint(w / np.where(sc > 0, sc, np.float32(1))), np.float32(0))
+    return np.clip(q, -127, 127).astype(np.int8), s
+
+
 def linear_f32(x, w, bf=False):
     x = np.ascontiguousarray(x, np.float32); w = np.ascontiguousarray(w, np.float32)
     y = np.empty((x.shape[0], w.shape[0]), np.float32)

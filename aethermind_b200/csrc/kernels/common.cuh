@@ -104,6 +104,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
             : "memory");
     return ok != 0;
 }
+// Non-blocking test of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+            "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+    return ok != 0;
+}
 // Bounded wait for the phase with the given parity; false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -111,6 +121,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     while (!mbar_try_wait(bar, parity))
         if (clock64() - t0 > kSpinLimitCycles) return false;
     return true;
+}
+// An L2 policy that evicts these lines first: for data read exactly once
+// (streamed weights), so it does not push out what is read again soon.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+// Global -> shared bulk copy with an L2 cache policy, completing on `bar`.
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+    asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+                    "r"(smem_u32(dst)),
+            "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+            : "memory");
 }
 // Global -> shared bulk copy completing on `bar` (16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

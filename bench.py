@@ -344,6 +344,8 @@ def main() -> None:
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--layers", type=int, default=None, help="debug: fewer layers (invalidates the number)")
     ap.add_argument("--no-extra", action="store_true", help="skip the other BASELINE workloads (bs=8, 1B W8, 70B W4)")
+    ap.add_argument("--decode", default="per-op", choices=["per-op", "persistent"],
+                    help="decode plan: one kernel per op, or the persistent all-layers kernel (batch 1)")
     ap.add_argument("--nccl-allreduce", action="store_true", help="TP: NCCL for every all-reduce (no peer-memory one-shot)")
     ap.add_argument("--op", default=None, help="time one kernel instead: gemv_gate_up | gemv_down | gemm_gate_up")
     ap.add_argument("--copies", type=int, default=None, help="--op gemv_*: weight copies rotated")
@@ -406,7 +408,7 @@ def main() -> None:
             args.nccl_allreduce = True
     model = session.Model(rt, cfg)
     model.init_synthetic(SEED)
-    sess = session.Session(model)
+    sess = session.Session(model, persistent_decode=args.decode == "persistent")
     prompt = np.random.default_rng(SEED).integers(0, cfg.vocab, PROMPT).astype(np.uint32)
 
     for _ in range(args.warmup):

@@ -100,28 +100,36 @@ def test_batch8_rows_equal_single_runs(sess_mod, rt):
 
 
 def test_persistent_decode_matches_per_op_plan(sess_mod, rt, oracle_lib):
-    """The persistent decode step (one launch for all layers, bs <= 2, INT4)
-    against the per-op decode plan and the oracle: same tokens up to a
-    documented near-tie (its GEMVs split K over 16 warps instead of 8, so
-    fp32 sums round differently)."""
+    """The persistent decode step (one launch for all layers, batch 1, INT4)
+    against the oracle and the per-op decode plan: every position compared
+    (near-tie flips allowed: its GEMVs sum in another order, so fp32 sums
+    round differently); eager and graph replay give the same tokens; batch 2
+    takes the per-op plan."""
     import dataclasses
-    cfg = dataclasses.replace(sess_mod.LLAMA_8B_W4, layers=3, max_seq=512, max_batch=2)
+    cfg = dataclasses.replace(sess_mod.LLAMA_8B_W4, layers=3, max_seq=1024, max_batch=2)
     m = sess_mod.Model(rt, cfg)
     m.init_synthetic(seed=1)
-    prompt = np.random.default_rng(9).integers(0, cfg.vocab, 24).astype(np.uint32)
+    # 300 prompt tokens: the attention phase splits the keys (256 per split)
+    prompt = np.random.default_rng(9).integers(0, cfg.vocab, 300).astype(np.uint32)
     s_p = sess_mod.Session(m, persistent_decode=True)
     assert any("DecodeStackPersistent" in l for l in s_p.plan_steps(1, 1, 1))
-    got = s_p.generate(prompt, 16)
-    ref, gaps = oracle_lib.synthetic_oracle_model(cfg, seed=1).generate(prompt.astype(np.int64), 16)
-    assert _compare(got.tolist(), ref.tolist(), gaps, 0.125) >= 8
-    per_op = sess_mod.Session(m).generate(prompt, 16)
-    assert _compare(got.tolist(), per_op.tolist(), gaps, 0.125) >= 8
-    # batch of 2 (two rows) and eager replay agree with the graph replay
-    p2 = np.stack([prompt, np.random.default_rng(10).integers(0, cfg.vocab, 24).astype(np.uint32)])
-    g2 = s_p.generate(p2, 8)
-    np.testing.assert_array_equal(g2[0], got[:8])
-    np.testing.assert_array_equal(sess_mod.Session(m, use_cuda_graph=False, persistent_decode=True).generate(prompt, 16),
+    assert not any("DecodeStackPersistent" in l for l in s_p.plan_steps(1, 2, 1))
+    ref, gaps = oracle_lib.synthetic_oracle_model(cfg, seed=1).generate(prompt.astype(np.int64), 24)
+    flips = walk_greedy(s_p, prompt, ref, gaps, NEAR_TIE_BF16)
+    assert len(flips) <= 4, f"near-tie flips at {flips}"
+    got = s_p.generate(prompt, 24)
+    per_op = sess_mod.Session(m).generate(prompt, 24)
+    assert _compare(got.tolist(), per_op.tolist(), gaps, NEAR_TIE_BF16) >= 8
+    np.testing.assert_array_equal(sess_mod.Session(m, use_cuda_graph=False, persistent_decode=True).generate(prompt, 24),
                                   got)
+    # a full 8B-depth stack (32 layers) on a short prompt against the per-op plan
+    cfg32 = dataclasses.replace(sess_mod.LLAMA_8B_W4, max_seq=128, max_batch=1)
+    m32 = sess_mod.Model(rt, cfg32)
+    m32.init_synthetic(seed=0)
+    p32 = np.random.default_rng(100).integers(0, cfg32.vocab, 16).astype(np.uint32)
+    a = sess_mod.Session(m32, persistent_decode=True).generate(p32, 16)
+    b = sess_mod.Session(m32).generate(p32, 16)
+    assert _compare(a.tolist(), b.tolist(), np.zeros(16), 1.0) >= 12
 
 
 def test_plan_resolves_phase_kernels(sess_mod, rt):

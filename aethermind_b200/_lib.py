@@ -56,7 +56,7 @@ class AmcuLinearArgs(C.Structure):
                 ("m", C.c_int64), ("x_stride", C.c_int64), ("y_stride", C.c_int64),
                 ("act_dtype", C.c_int32), ("epilogue", C.c_int32), ("workspace", C.c_void_p),
                 ("workspace_size", C.c_size_t), ("norm_weight", C.c_void_p), ("norm_eps", C.c_float),
-                ("l2_next", AmcuL2Prefetch)]
+                ("l2_next", AmcuL2Prefetch), ("peer_reduce", C.c_void_p)]
 
 
 class AmcuRopeKvArgs(C.Structure):

@@ -21,6 +21,8 @@
 //      acquire loads;
 //   4. sum the local partial and the peers' chunks from the local mailbox,
 //      add the residual, store x; epochs[c] = e.
+// The area also holds the region of the GEMV-epilogue all-reduce
+// (allreduce.cuh, ar_fuse_*), which follows the same protocol per row block.
 // Two parities suffice: a rank writes parity (e+1) & 1 only after finishing
 // call e, and cannot start call e+2 before every peer has written call e+1,
 // i.e. finished reading parity e & 1.
@@ -54,7 +56,7 @@ __host__ __device__ inline size_t ar_mailbox_offset(int parity, int src, int64_t
 }
 __host__ __device__ constexpr size_t ar_flags_offset() { return (size_t)2 * kArMaxRanks * kArMaxElems * 2; }
 __host__ __device__ constexpr size_t ar_epochs_offset() { return ar_flags_offset() + (size_t)kArMaxRanks * kArMaxCtas * 4; }
-size_t ar_area_bytes() { return ar_epochs_offset() + (size_t)kArMaxCtas * 4; }
+size_t ar_area_bytes() { return ar_fuse_epochs_offset() + (size_t)kFuseMaxRb * 4; }
 
 __global__ void __launch_bounds__(kArThreads) ar_oneshot_add_kernel(ArParams p) {
     const int c = blockIdx.x, tid = threadIdx.x;

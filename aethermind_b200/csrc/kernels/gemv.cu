@@ -25,6 +25,7 @@
 // 8-15 the matching up rows, so one lane holds gate and up of the same output
 // and the SiLU-Mul epilogue needs no data exchange.
 #include "../amcu_internal.h"
+#include "allreduce.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 #include "gemv_stage.cuh"
@@ -34,6 +35,98 @@ namespace amcu {
 
 template <typename T>
 __device__ __forceinline__ T epi_store(float v) { return Act<T>::store(v); }
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* a, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* a) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t gemv_clock_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+constexpr int32_t kErrGemvPeerWait = 0x402;
+
+// Tensor-parallel o/down epilogue: y = round(residual + round(sum_r p_r)), the
+// sum over the ranks' fp32 partials p_r of this row block, exchanged over peer
+// memory by this warp alone (every rank's CTA owns the same row blocks):
+//   1. e = epoch[rb] + 1; push this rank's partials into every peer's mailbox
+//      (parity e & 1, slot of this rank), fence at system scope, release-store
+//      e into each peer's flag of (this rank, rb);
+//   2. wait (bounded) until every peer's flag of rb here is >= e;
+//   3. sum the ranks' partials in rank order (the same order on every rank),
+//      round, add the residual, store; epoch[rb] = e.
+// Two parities suffice as in the one-shot all-reduce: a rank overwrites a
+// parity only after its wait in the next call proved every peer finished
+// reading it. Lane (g, t): rows g and g+8 of the block, activation rows 2t,
+// 2t+1; the mailbox keeps [row][activation row < 8].
+__device__ __noinline__ void gemv_peer_sum_epilogue(const GemvParams& p, int64_t rb, int g, int t, const float (&acc)[4]) {
+    const int lane = (g << 2) | t, rank = p.fuse.rank, world = p.fuse.world;
+    uint8_t* own = p.fuse.area[rank];
+    uint32_t* epochs = reinterpret_cast<uint32_t*>(own + ar_fuse_epochs_offset());
+    const uint32_t e = epochs[rb] + 1;
+    const int par = (int)(e & 1u);
+    const int64_t n_lo = rb * 16 + g, n_hi = n_lo + 8;
+    const int64_t i_lo = n_lo * 8 + 2 * t, i_hi = n_hi * 8 + 2 * t;
+    const float2 v_lo = make_float2(acc[0], acc[1]), v_hi = make_float2(acc[2], acc[3]);
+    for (int q = 0; q < world; ++q) {
+        if (q == rank) continue;
+        uint8_t* pa = p.fuse.area[q];
+        *reinterpret_cast<float2*>(pa + ar_fuse_mail_offset(par, rank, i_lo)) = v_lo;
+        *reinterpret_cast<float2*>(pa + ar_fuse_mail_offset(par, rank, i_hi)) = v_hi;
+    }
+    // the warp's stores precede lane 0's release (__syncwarp orders them), and
+    // a release is cumulative: one release store per peer publishes them all
+    __syncwarp();
+    if (lane == 0)
+        for (int q = 0; q < world; ++q)
+            if (q != rank)
+                st_release_sys_u32(reinterpret_cast<uint32_t*>(p.fuse.area[q] + ar_fuse_flags_offset()) +
+                                           rank * kFuseMaxRb + rb,
+                                   e);
+    if (lane < world && lane != rank) {
+        const uint32_t* f = reinterpret_cast<const uint32_t*>(own + ar_fuse_flags_offset()) + lane * kFuseMaxRb + rb;
+        const uint64_t t0 = gemv_clock_ns();
+        while ((int32_t)(ld_acquire_sys_u32(f) - e) < 0) {
+            if (gemv_clock_ns() - t0 > p.fuse.wait_ns) {
+                record_device_error(p.err, kErrGemvPeerWait);
+                break;
+            }
+        }
+    }
+    __syncwarp();
+    float2 s_lo = make_float2(0.f, 0.f), s_hi = make_float2(0.f, 0.f);
+    for (int q = 0; q < world; ++q) {
+        float2 a, b;
+        if (q == rank) {
+            a = v_lo;
+            b = v_hi;
+        } else {
+            a = __ldcv(reinterpret_cast<const float2*>(own + ar_fuse_mail_offset(par, q, i_lo)));
+            b = __ldcv(reinterpret_cast<const float2*>(own + ar_fuse_mail_offset(par, q, i_hi)));
+        }
+        s_lo.x += a.x; s_lo.y += a.y;
+        s_hi.x += b.x; s_hi.y += b.y;
+    }
+    __nv_bfloat16* y = static_cast<__nv_bfloat16*>(p.y);
+    const __nv_bfloat16* res = static_cast<const __nv_bfloat16*>(p.residual);
+    const float v[4] = {s_lo.x, s_lo.y, s_hi.x, s_hi.y};
+    const int ms[4] = {2 * t, 2 * t + 1, 2 * t, 2 * t + 1};
+    const int64_t ns[4] = {n_lo, n_lo, n_hi, n_hi};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (ms[i] < p.m) {
+            const int64_t off = ms[i] * p.y_stride + ns[i];
+            y[off] = __float2bfloat16_rn(Act<__nv_bfloat16>::round(v[i]) + __bfloat162float(res[off]));
+        }
+    }
+    __syncwarp();
+    if (lane == 0) epochs[rb] = e;
+}
 
 // rm0 / rm1: exact power-of-two multipliers of activation rows 2t and 2t+1
 // (undo the staging's overflow guard).
@@ -51,6 +144,12 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int64_t rb, i
         acc[1] *= s_lo;
         acc[2] *= s_hi;
         acc[3] *= s_hi;
+    }
+    if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD) {
+        if (p.fuse.world > 1) {
+            gemv_peer_sum_epilogue(p, rb, g, t, acc);
+            return;
+        }
     }
     if constexpr (EPI == AMCU_EPI_SILU_MUL) {
         // c0/c1: gate row, c2/c3: up row of output column 8*rb + g.

@@ -27,6 +27,13 @@ struct GemvParams {
     int stages;          // shared-memory ring stages (set by the launcher)
     int stage_units;     // 128-column group units per stage (set by the launcher)
     AmcuL2Prefetch l2_next;  // ranges the next operation reads (hint)
+    // Tensor-parallel RESIDUAL_ADD: partials summed over the ranks in the
+    // epilogue (world 0 = off); every rank's exchange area as mapped here.
+    struct {
+        uint8_t* area[8];
+        int rank, world;
+        uint64_t wait_ns;
+    } fuse;
 };
 
 // Quantized (INT4 / INT8 tile16x64) GEMV, m <= kGemvMaxM, bf16 activations.

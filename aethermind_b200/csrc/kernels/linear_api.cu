@@ -1,6 +1,7 @@
 // C-ABI entry points of the Linear family: argument validation and the
 // m-based dispatch between the decode GEMV and the prefill GEMM.
 #include "../amcu_internal.h"
+#include "allreduce.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
 
@@ -35,6 +36,16 @@ am_status_code validate_linear(const AmcuLinearArgs* a, const char* who) {
         const int64_t xs = a->x_stride ? a->x_stride : w.k;
         AMCU_REQUIRE(xs % 8 == 0, "%s: x row stride must be a multiple of 8 elements", who);
     }
+    if (const AmcuAllReduceArgs* pr = a->peer_reduce) {
+        AMCU_REQUIRE(a->epilogue == AMCU_EPI_RESIDUAL_ADD && w.format != AMCU_WFMT_PLAIN && a->m <= kGemvMaxM,
+                     "%s: peer_reduce needs a quantized GEMV (m <= %d) with the residual epilogue", who, kGemvMaxM);
+        AMCU_REQUIRE(pr->world >= 2 && pr->world <= kArMaxRanks && pr->rank >= 0 && pr->rank < pr->world,
+                     "%s: peer_reduce rank/world out of range", who);
+        AMCU_REQUIRE(w.n * kGemvMaxM <= kFuseMaxVals && w.n / 16 <= kFuseMaxRb,
+                     "%s: peer_reduce supports at most %lld output rows", who, (long long)(kFuseMaxVals / kGemvMaxM));
+        for (int r = 0; r < pr->world; ++r)
+            AMCU_REQUIRE(pr->areas[r] != nullptr, "%s: peer_reduce area %d missing", who, r);
+    }
     return AM_STATUS_OK;
 }
 
@@ -54,6 +65,12 @@ GemvParams make_params(const AmcuLinearArgs* a) {
     p.norm_w = a->norm_weight;
     p.eps = a->norm_eps;
     p.l2_next = a->l2_next;
+    if (const AmcuAllReduceArgs* pr = a->peer_reduce) {
+        for (int r = 0; r < pr->world; ++r) p.fuse.area[r] = static_cast<uint8_t*>(pr->areas[r]);
+        p.fuse.rank = pr->rank;
+        p.fuse.world = pr->world;
+        p.fuse.wait_ns = pr->wait_limit_us ? pr->wait_limit_us * 1000ull : 2000000000ull;
+    }
     return p;
 }
 
@@ -73,6 +90,7 @@ am_status_code run_gemv(const AmcuLinearArgs* a, cudaStream_t s) {
 }
 
 am_status_code run_gemm(const AmcuLinearArgs* a, cudaStream_t s) {
+    AMCU_REQUIRE(a->peer_reduce == nullptr, "amcu_linear: peer_reduce is for the decode GEMV (m <= %d)", kGemvMaxM);
     if (a->w.format == AMCU_WFMT_PLAIN) {
         launch_gemm_plain(make_params(a), a->act_dtype, a->epilogue, s);
         return check_launch("amcu_gemm_plain");

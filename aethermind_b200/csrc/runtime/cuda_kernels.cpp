@@ -86,6 +86,7 @@ Status BuildLinear(std::span<const TensorView> in, std::span<const MutableTensor
     if (at) {
         a->norm_weight = at->norm_weight;
         a->norm_eps = at->norm_eps;
+        a->peer_reduce = at->peer_reduce;
     }
     if (in.size() > 1) a->residual = in[1].data;
     return Status::Ok();

@@ -359,6 +359,11 @@ Status Communicator::OpenPeers(const void* handles) {
         }
     }
     peers_open_ = true;
+    peer_args_ = AmcuAllReduceArgs{};
+    peer_args_.rank = rank_;
+    peer_args_.world = world_;
+    for (int r = 0; r < world_; ++r) peer_args_.areas[r] = peers_[r];
+    peer_args_.wait_limit_us = wait_ns_ / 1000;
     return Status::Ok();
 }
 

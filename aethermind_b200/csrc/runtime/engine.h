@@ -203,6 +203,9 @@ public:
     Status AllReduceAddBf16(const void* part, void* x, int64_t n, cudaStream_t s);
     // Bound of the one-shot all-reduce's wait for the peers (0: about 2 s).
     void set_wait_ns(uint64_t ns) { wait_ns_ = ns; }
+    // The peer areas for a GEMV whose epilogue sums the ranks' partials
+    // (AmcuLinearArgs::peer_reduce); null until OpenPeers succeeded.
+    const AmcuAllReduceArgs* PeerReduceArgs() const { return peers_open_ ? &peer_args_ : nullptr; }
 
 private:
     void* comm_ = nullptr;
@@ -211,6 +214,7 @@ private:
     void* peers_[8] = {};           // every rank's area as mapped here
     bool peers_open_ = false;
     uint64_t wait_ns_ = 0;
+    AmcuAllReduceArgs peer_args_{};
 };
 Status NcclGetUniqueId(void* out128);
 

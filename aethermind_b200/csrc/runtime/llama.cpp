@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -591,6 +592,23 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
                 LinearAttrs res{AMCU_EPI_RESIDUAL_ADD};
                 return pb.Add(OpType::kLinear, lin, {in, View2(s->x.data(), A, M, H, H)}, {MView2(s->x.data(), A, M, H, H)},
                               &res, &W.w, p + name);
+            }
+            // decode GEMV: the ranks' partials are summed over peer memory in
+            // the GEMV's own epilogue, residual added there (one launch)
+            // Opt-in (AMCU_TP_FUSED_ALLREDUCE=1): on 2 B200s the 8B decode step
+            // measured 2.15 ms/token with the exchange in the GEMV epilogue
+            // against 1.94 with the separate one-shot kernel, whose small grid
+            // lets the next GEMV's CTAs start streaming during the exchange.
+            static const bool fused_ok = [] {
+                const char* v = std::getenv("AMCU_TP_FUSED_ALLREDUCE");
+                return v && v[0] == '1';
+            }();
+            if (fused_ok && phase == ExecPhase::kDecode && M <= 8 && wf != WeightFormat::kPlain && A == DType::kBF16 &&
+                m->rt->comm.PeerReduceArgs() != nullptr && H * 8 <= 16384 * 8) {
+                LinearAttrs res{AMCU_EPI_RESIDUAL_ADD};
+                res.peer_reduce = m->rt->comm.PeerReduceArgs();
+                return pb.Add(OpType::kLinear, lin, {in, View2(s->x.data(), A, M, H, H)},
+                              {MView2(s->x.data(), A, M, H, H)}, &res, &W.w, p + name + "+allreduce(peer)");
             }
             AM_RETURN_IF_ERROR(pb.Add(OpType::kLinear, lin, {in}, {MView2(s->part.data(), A, M, H, H)}, &store, &W.w,
                                       p + name + "_partial"));

@@ -12,6 +12,7 @@ struct LinearAttrs {
     int32_t epilogue;                  // amcu_epilogue
     const void* norm_weight = nullptr;  // fused RMSNorm of the input (decode GEMV)
     float norm_eps = 0.f;
+    const AmcuAllReduceArgs* peer_reduce = nullptr;  // tensor-parallel o/down: ranks summed in the epilogue
 };
 struct RopeKvAttrs {
     double theta;

@@ -221,6 +221,12 @@ typedef struct AmcuLinearArgs {
                                 (the RMSNorm that precedes q/k/v and gate/up, fused) */
     float norm_eps;
     AmcuL2Prefetch l2_next;  /* optional: ranges the next operation reads */
+    /* optional, tensor parallel, GEMV (m <= 8) with EPI_RESIDUAL_ADD only: the
+     * ranks' partial products are summed over peer memory inside the GEMV's
+     * epilogue, y = round(residual + round(sum over ranks of W_r x_r)), with no
+     * separate all-reduce launch (areas, rank, world and wait_limit_us of
+     * amcu_allreduce_oneshot_add are used; part, x and n are ignored). */
+    const struct AmcuAllReduceArgs* peer_reduce;
 } AmcuLinearArgs;
 /* Dispatches on m: GEMV (m <= 8) or the tensor-core GEMM (m > 8). */
 am_status_code amcu_linear(const AmcuLinearArgs* args, void* stream);

@@ -48,8 +48,12 @@ def _run(peer, port, tmp):
     mp.start_processes(_rank, args=(2, port, peer, str(tmp)), nprocs=2, join=True, start_method="spawn")
 
 
-@pytest.mark.parametrize("peer", [True, False])
-def test_tp2_matches_one_gpu(built_lib, oracle_lib, tmp_path, peer):
+@pytest.mark.parametrize("peer,fused", [(True, False), (True, True), (False, False)])
+def test_tp2_matches_one_gpu(built_lib, oracle_lib, tmp_path, monkeypatch, peer, fused):
+    """peer: decode all-reduces over peer memory (else NCCL); fused: the sum
+    runs inside the o/down GEMV's epilogue (AmcuLinearArgs::peer_reduce)
+    instead of a separate one-shot kernel."""
+    monkeypatch.setenv("AMCU_TP_FUSED_ALLREDUCE", "1" if fused else "0")
     import dataclasses
 
     import torch
@@ -59,7 +63,7 @@ def test_tp2_matches_one_gpu(built_lib, oracle_lib, tmp_path, peer):
     from aethermind_b200 import session
     from tests.test_model_gpu import _compare
 
-    _run(peer, 29611 + int(peer), tmp_path)
+    _run(peer, 29611 + int(peer) + 2 * int(fused), tmp_path)
     got = np.load(tmp_path / f"tp_{int(peer)}.npy")
     got2 = np.load(tmp_path / f"tp2_{int(peer)}.npy")
     cfg = dataclasses.replace(session.LLAMA_8B_W4, layers=2, max_seq=256, max_batch=2)

@@ -50,6 +50,9 @@ __device__ __forceinline__ uint64_t gemv_clock_ns() {
     return t;
 }
 constexpr int32_t kErrGemvPeerWait = 0x402;
+// The residual epilogue with the tensor-parallel sum over the ranks: its own
+// kernel instantiation, so the single-GPU residual kernel keeps its code.
+constexpr int kEpiResidualPeer = 3;
 
 // Tensor-parallel o/down epilogue: y = round(residual + round(sum_r p_r)), the
 // sum over the ranks' fp32 partials p_r of this row block, exchanged over peer
@@ -64,7 +67,7 @@ constexpr int32_t kErrGemvPeerWait = 0x402;
 // parity only after its wait in the next call proved every peer finished
 // reading it. Lane (g, t): rows g and g+8 of the block, activation rows 2t,
 // 2t+1; the mailbox keeps [row][activation row < 8].
-__device__ __noinline__ void gemv_peer_sum_epilogue(const GemvParams& p, int64_t rb, int g, int t, const float (&acc)[4]) {
+__device__ __forceinline__ void gemv_peer_sum_epilogue(const GemvParams& p, int64_t rb, int g, int t, const float (&acc)[4]) {
     const int lane = (g << 2) | t, rank = p.fuse.rank, world = p.fuse.world;
     uint8_t* own = p.fuse.area[rank];
     uint32_t* epochs = reinterpret_cast<uint32_t*>(own + ar_fuse_epochs_offset());
@@ -145,11 +148,9 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int64_t rb, i
         acc[2] *= s_hi;
         acc[3] *= s_hi;
     }
-    if constexpr (EPI == AMCU_EPI_RESIDUAL_ADD) {
-        if (p.fuse.world > 1) {
-            gemv_peer_sum_epilogue(p, rb, g, t, acc);
-            return;
-        }
+    if constexpr (EPI == kEpiResidualPeer) {
+        gemv_peer_sum_epilogue(p, rb, g, t, acc);
+        return;
     }
     if constexpr (EPI == AMCU_EPI_SILU_MUL) {
         // c0/c1: gate row, c2/c3: up row of output column 8*rb + g.
@@ -503,7 +504,10 @@ template <int FMT>
 static void launch_gemv_fmt(const GemvParams& p, int epi, cudaStream_t s) {
     switch (epi) {
         case AMCU_EPI_STORE: launch_gemv_one<FMT, AMCU_EPI_STORE>(p, s); break;
-        case AMCU_EPI_RESIDUAL_ADD: launch_gemv_one<FMT, AMCU_EPI_RESIDUAL_ADD>(p, s); break;
+        case AMCU_EPI_RESIDUAL_ADD:
+            if (p.fuse.world > 1) launch_gemv_one<FMT, kEpiResidualPeer>(p, s);
+            else launch_gemv_one<FMT, AMCU_EPI_RESIDUAL_ADD>(p, s);
+            break;
         default: launch_gemv_one<FMT, AMCU_EPI_SILU_MUL>(p, s); break;
     }
 }

@@ -595,13 +595,12 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
             }
             // decode GEMV: the ranks' partials are summed over peer memory in
             // the GEMV's own epilogue, residual added there (one launch)
-            // Opt-in (AMCU_TP_FUSED_ALLREDUCE=1): on 2 B200s the 8B decode step
-            // measured 2.15 ms/token with the exchange in the GEMV epilogue
-            // against 1.94 with the separate one-shot kernel, whose small grid
-            // lets the next GEMV's CTAs start streaming during the exchange.
+            // On by default (AMCU_TP_FUSED_ALLREDUCE=0 selects the separate
+            // one-shot kernel): on 2 B200s the 8B decode step measured 1.937
+            // ms/token fused, 1.941 with the one-shot kernel, 2.035 with NCCL.
             static const bool fused_ok = [] {
                 const char* v = std::getenv("AMCU_TP_FUSED_ALLREDUCE");
-                return v && v[0] == '1';
+                return !(v && v[0] == '0');
             }();
             if (fused_ok && phase == ExecPhase::kDecode && M <= 8 && wf != WeightFormat::kPlain && A == DType::kBF16 &&
                 m->rt->comm.PeerReduceArgs() != nullptr && H * 8 <= 16384 * 8) {

@@ -459,44 +459,61 @@ __global__ void gemm_plain_kernel(GemvParams p) {
 
 template <int FMT, int EPI>
 static void launch_gemv_one(GemvParams p, cudaStream_t s) {
-    constexpr int kMaxSmem = 200 * 1024;
+    constexpr int kMaxSmem = 224 * 1024;
     const int smem_sm = smem_per_sm();
     set_func_attr_once((const void*)gemv_tc_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
     constexpr int UB = FMT == AMCU_WFMT_INT4 ? kW4PairBytes : 2048;
-    const int per_cta = smem_sm / GEMV_CPS - 2048;  // room for the per-CTA reserve
-    int su = stage_units<FMT>(p.k);
-    // long rows (one activation row of K above ~24K columns): the large stages
-    // would leave room for one CTA per SM, so they go back to 16 records
-    if (FMT == AMCU_WFMT_INT4 && gemv_smem<FMT>(1, p.k, su * UB, 2).total > per_cta) su = stage_units<FMT>(p.k, 16);
-    const int sby = su * UB;
-    // Ring stages: as many (2..8) as keep GEMV_CPS CTAs resident per SM with
-    // one activation row.
-    int stages = 8;
-    while (stages > 2 && gemv_smem<FMT>(1, p.k, sby, stages).total > per_cta) --stages;
-    p.stages = stages;
-    p.stage_units = su;
-    int per_sm = smem_sm / (gemv_smem<FMT>(1, p.k, sby, stages).total + 1024);
-#ifdef GEMV_GRID_CPS
-    // size the grid for fewer CTAs per SM than fit, leaving room for the next
-    // kernel's CTAs to start (and stream their weights) early
-    if (per_sm > GEMV_GRID_CPS) per_sm = GEMV_GRID_CPS;
-#endif
-    const int64_t max_ctas = (int64_t)(per_sm > 0 ? per_sm : 1) * num_sms();
-    const int64_t nrb = p.n / 16;
-    p.rb_per_cta = (int)((nrb + max_ctas - 1) / max_ctas);
-    const int64_t grid = (nrb + p.rb_per_cta - 1) / p.rb_per_cta;
-    // The activation rows are staged in shared memory; when m rows of this K do
-    // not fit next to the ring, the rows go in slices (each slice streams W again).
+    const int per_cta2 = smem_sm / GEMV_CPS - 2048;  // GEMV_CPS CTAs per SM (room for the per-CTA reserve)
+    const int per_cta1 = kMaxSmem;                  // one CTA per SM
+    // The activation rows are staged in shared memory; when the m rows of this
+    // K do not fit beside a ring of two 16-record stages, they go in equal
+    // slices (each slice streams W again).
     int64_t fit = p.m;
-    while (fit > 1 && gemv_smem<FMT>((int)fit, p.k, sby, stages).total > kMaxSmem) --fit;
+    while (fit > 1 && gemv_smem<FMT>((int)fit, p.k, stage_units<FMT>(p.k, 16) * UB, 2).total > per_cta1) --fit;
+    {
+        const int64_t slices = (p.m + fit - 1) / fit;
+        fit = (p.m + slices - 1) / slices;
+    }
+    // Ring geometry for a slice of `rows`: GEMV_CPS CTAs per SM with the
+    // largest stages (up to 32 records; 16 or 8 when the rows are long) that
+    // leave two of them; else one CTA per SM with as many stages (2..8) as
+    // fit. The grid is sized for the CTAs resident at once, so no CTA waits
+    // for a second wave.
+    auto plan = [&](int rows, int& su, int& stages, int& per_sm) {
+        for (int cap : {0, 16, 8}) {
+            su = stage_units<FMT>(p.k, cap);
+            if (gemv_smem<FMT>(rows, p.k, su * UB, 2).total <= per_cta2) {
+                stages = 8;
+                while (stages > 2 && gemv_smem<FMT>(rows, p.k, su * UB, stages).total > per_cta2) --stages;
+                per_sm = smem_sm / (gemv_smem<FMT>(rows, p.k, su * UB, stages).total + 1024);
+                return;
+            }
+        }
+        su = stage_units<FMT>(p.k);
+        if (gemv_smem<FMT>(rows, p.k, su * UB, 2).total > per_cta1) su = stage_units<FMT>(p.k, 16);
+        stages = 8;
+        while (stages > 2 && gemv_smem<FMT>(rows, p.k, su * UB, stages).total > per_cta1) --stages;
+        per_sm = 1;
+    };
+    const int64_t nrb = p.n / 16;
     for (int64_t m0 = 0; m0 < p.m; m0 += fit) {
         GemvParams q = p;
         q.m = p.m - m0 < fit ? p.m - m0 : fit;
+        int su = 0, stages = 0, per_sm = 1;
+        plan((int)q.m, su, stages, per_sm);
+#ifdef GEMV_GRID_CPS
+        if (per_sm > GEMV_GRID_CPS) per_sm = GEMV_GRID_CPS;
+#endif
+        q.stages = stages;
+        q.stage_units = su;
+        const int64_t max_ctas = (int64_t)(per_sm > 0 ? per_sm : 1) * num_sms();
+        q.rb_per_cta = (int)((nrb + max_ctas - 1) / max_ctas);
+        const int64_t grid = (nrb + q.rb_per_cta - 1) / q.rb_per_cta;
         q.x = static_cast<const __nv_bfloat16*>(p.x) + m0 * p.x_stride;
         q.y = static_cast<__nv_bfloat16*>(p.y) + m0 * p.y_stride;
         if (p.residual) q.residual = static_cast<const __nv_bfloat16*>(p.residual) + m0 * p.y_stride;
         launch_pdl(gemv_tc_kernel<FMT, EPI>, dim3((unsigned)grid), dim3(kGemvThreads),
-                   (size_t)gemv_smem<FMT>((int)q.m, p.k, sby, stages).total, s, q);
+                   (size_t)gemv_smem<FMT>((int)q.m, p.k, su * UB, stages).total, s, q);
     }
 }
 

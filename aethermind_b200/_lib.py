@@ -181,6 +181,7 @@ _SIGS = {
     "am_debug_kv_offset": (C.c_int, [C.c_uint64] * 4 + [C.c_int32] + [C.c_uint64] * 6 +
                            [C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "am_debug_kv_reserve": (C.c_int, [C.c_uint64] * 3),
+    "am_debug_tp_shard": (C.c_int, [C.c_char_p, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.POINTER(C.c_int64)]),
 }
 
 _lib = None

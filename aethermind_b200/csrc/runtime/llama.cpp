@@ -187,20 +187,33 @@ Status PackInto(am_model_s* m, LinearWeight& lw, int64_t row0, const Canon& cn) 
 
 enum class Split { kNone, kRows, kCols };
 
+// This rank's block of an [n, k] tensor under a split: rows [r0, r0 + nr) x
+// columns [c0, c0 + nc). Rows: column-parallel (q/k/v by heads, gate/up by
+// intermediate columns); columns: row-parallel (o, down), at boundaries that
+// stay multiples of 128 when the shapes are (checked at model creation).
+void ShardRange(Split sp, int64_t n, int64_t k, int r, int w, int64_t& r0, int64_t& nr, int64_t& c0, int64_t& nc) {
+    r0 = 0, nr = n, c0 = 0, nc = k;
+    if (w <= 1 || sp == Split::kNone) return;
+    if (sp == Split::kRows) {
+        nr = n / w;
+        r0 = r * nr;
+    } else {
+        nc = k / w;
+        c0 = r * nc;
+    }
+}
+
 // Full canonical tensor (device) -> this rank's shard.
 Status Shard(am_model_s* m, Canon& full, Split sp, int64_t unit, Canon& out) {
     const int r = m->rt->tp_rank, w = m->rt->tp_size;
+    (void)unit;
     if (w == 1 || sp == Split::kNone) {
         out = std::move(full);
         return Status::Ok();
     }
-    if (sp == Split::kRows) {
-        const int64_t nr = full.n / w;
-        (void)unit;
-        return SliceCanon(m, full, r * nr, nr, 0, full.k, out);
-    }
-    const int64_t nc = full.k / w;
-    return SliceCanon(m, full, 0, full.n, r * nc, nc, out);
+    int64_t r0, nr, c0, nc;
+    ShardRange(sp, full.n, full.k, r, w, r0, nr, c0, nc);
+    return SliceCanon(m, full, r0, nr, c0, nc, out);
 }
 
 Status UploadCanon(am_model_s* m, int64_t n, int64_t k, const void* hq, const void* hs, Canon& out) {
@@ -1398,6 +1411,20 @@ am_status_code am_debug_kv_offset(uint64_t layers, uint64_t heads, uint64_t max_
     if (!off.ok()) return Fail(off.status());
     if (offset) *offset = off.value();
     if (bytes_per_plane) *bytes_per_plane = mgr.layout().BytesPerPlane().value();
+    return AM_STATUS_OK;
+}
+
+am_status_code am_debug_tp_shard(const char* tensor, int64_t n, int64_t k, int32_t rank, int32_t world,
+                                 int64_t* out4) {
+    if (!tensor || !out4 || world < 1 || rank < 0 || rank >= world)
+        return Fail(Status::InvalidArgument("am_debug_tp_shard: bad arguments"));
+    const std::string t(tensor);
+    Split sp;
+    if (t == "wq" || t == "wk" || t == "wv" || t == "wg" || t == "wu") sp = Split::kRows;
+    else if (t == "wo" || t == "wd") sp = Split::kCols;
+    else if (t == "embed" || t == "lm_head" || t == "attn_norm" || t == "mlp_norm" || t == "final_norm") sp = Split::kNone;
+    else return Fail(Status::NotFound("am_debug_tp_shard: unknown tensor " + t));
+    ShardRange(sp, n, k, rank, world, out4[0], out4[1], out4[2], out4[3]);
     return AM_STATUS_OK;
 }
 

@@ -569,6 +569,12 @@ am_status_code am_debug_kv_offset(uint64_t layers, uint64_t kv_heads, uint64_t m
                                   uint64_t dim, uint64_t slot, uint64_t* offset, uint64_t* bytes_per_plane);
 /* Session reservation contract of the KV manager (capacity checks only). */
 am_status_code am_debug_kv_reserve(uint64_t max_tokens, uint64_t prompt_len, uint64_t max_new);
+/* The tensor-parallel block a rank keeps of a full [n, k] layer tensor
+ * ("wq".."wd", norms, "embed", "lm_head"): out4 = {row0, rows, col0, cols},
+ * the same rule the model uses when it shards weights (no reference
+ * counterpart; the reference runs on one device). Host only. */
+am_status_code am_debug_tp_shard(const char* tensor, int64_t n, int64_t k, int32_t rank, int32_t world,
+                                 int64_t* out4);
 
 #ifdef __cplusplus
 }

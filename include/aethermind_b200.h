@@ -71,7 +71,10 @@ const char* amcu_last_error(void);
 const char* amcu_version(void);
 /* Device error word of the current device: non-zero when a kernel's bounded
  * wait ran out (the kernel recorded a code and returned instead of hanging).
- * clear != 0 resets it. Synchronizes with the device. */
+ * clear != 0 resets it. Synchronizes with the device. The library caches the
+ * word's device address per device on first use: after cudaDeviceReset on a
+ * device, kernels of this library and this call must not be used on it again
+ * in the same process (the cached address belongs to the destroyed context). */
 am_status_code amcu_device_error(int32_t* code, int32_t clear);
 
 /* Element types (subset of the reference DataType used on the path). */
@@ -361,7 +364,9 @@ am_status_code amcu_attn_prefill(const AmcuAttentionArgs* args, void* stream);
  * rejected with AM_STATUS_INVALID_ARGUMENT. The first call on a device looks
  * up the scratch's device address; make that first call before any stream
  * capture. All calls share the one scratch: calls that overlap on the GPU
- * (e.g. on different streams) race and must be serialized by the caller. */
+ * (e.g. on different streams) race and must be serialized by the caller.
+ * The scratch address is cached per device for the life of the process:
+ * do not call this after cudaDeviceReset on that device. */
 am_status_code amcu_attn_decode_noalloc(const AmcuAttentionArgs* args, void* stream);
 
 /* ------------------------------------------------------------------------ */

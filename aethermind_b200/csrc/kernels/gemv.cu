@@ -184,14 +184,14 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int64_t rb, i
 // Streaming GEMV. A CTA of 8 consumer warps and 1 producer warp owns
 // `rb_per_cta` consecutive row blocks (16 output rows each), one contiguous
 // run of the packed weight. The producer streams that run through a ring of
-// `stages` shared-memory stages with bulk copies (TMA engine) of 8-17 KB --
+// `stages` shared-memory stages with bulk copies (TMA engine) of 8-33 KB --
 // copies that small stop being able to keep HBM busy -- completing on one
-// mbarrier per stage; the consumers release a stage on a second mbarrier.
-// The first stages are requested before the kernel waits for its
-// predecessor. In a stage the consumer warps split the 128-column groups
-// (INT4 pair records, INT8 tile pairs) and read their tiles with one
-// conflict-free shared load per lane per tile. The activations (m <= 8 rows,
-// bf16) are staged once per CTA in shared memory.
+// mbarrier per stage; the consumers release a stage on a second mbarrier. The first stages are
+// requested before the kernel waits for its predecessor. In a stage the
+// consumer warps split the 128-column groups (INT4 pair records, INT8 tile
+// pairs) and read their tiles with one conflict-free shared load per lane per
+// tile. The activations (m <= 8 rows, bf16) are staged once per CTA in shared
+// memory.
 //
 // INT4 tiles go to fp16 MMAs as exact integers with an offset: one LOP3
 // selects two nibbles and ORs in the fp16 exponent of 1024, giving 1032 + q
@@ -207,6 +207,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int64_t rb, i
 //
 // At the end of a row block the warps' 16 x 8 partial tiles meet in shared
 // memory (double-buffered, one barrier) and one warp applies the epilogue.
+//
+// The grid covers the CTA slots of all SMs only as far as whole row blocks
+// allow (e.g. 256 CTAs for 1792 row blocks on 296 slots). Dealing the groups
+// to all 296 slots in equal ranges cut inside row blocks (a split-K with a
+// last-arriver combine) measured slower, 17.4 against 13.3 us for the 8B
+// gate/up: the free slots let the next kernel's CTAs start early under PDL and
+// fetch their weights while this one finishes, which outweighs the balance.
 constexpr int kXPad = 16;  // bytes of padding per staged activation row
 #ifndef GEMV_MINB
 #define GEMV_MINB 2
@@ -233,7 +240,96 @@ __host__ __device__ inline GemvSmem gemv_smem(int m, int64_t k, int stage_bytes,
     return s;
 }
 
-template <int FMT, int EPI>
+// One 128-column group unit: `rec` is its record in the ring, `grp` its group
+// within the row block, xrow_g this lane's activation bytes of group 0 (+256
+// per group), sx the per-group activation sums (INT4). M1: one activation row
+// (m = 1): output column 2t + 1 of the MMA tile is never stored, so its
+// accumulators are not kept.
+template <int FMT, bool M1>
+__device__ __forceinline__ void gemv_unit(const uint8_t* rec, const uint8_t* xrow_g, const float* sx, int grp,
+                                          int lane, int g, int t, float (&acc)[4]) {
+    constexpr bool W4 = FMT == AMCU_WFMT_INT4;
+    const uint8_t* xp = xrow_g + grp * 256;
+    float part[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) part[h][e] = 0.f;
+        const uint4 x0 = *reinterpret_cast<const uint4*>(xp + h * 128);
+        const uint4 x1 = *reinterpret_cast<const uint4*>(xp + h * 128 + 16);
+        if constexpr (W4) {
+            const uint4 wv = *reinterpret_cast<const uint4*>(rec + h * 512 + lane * 16);
+            uint32_t a[4];
+            unpack_w4_word_f16(wv.x, a);
+            mma_f16_16816(part[h], a, x0.x, x0.y);
+            unpack_w4_word_f16(wv.y, a);
+            mma_f16_16816(part[h], a, x0.z, x0.w);
+            unpack_w4_word_f16(wv.z, a);
+            mma_f16_16816(part[h], a, x1.x, x1.y);
+            unpack_w4_word_f16(wv.w, a);
+            mma_f16_16816(part[h], a, x1.z, x1.w);
+        } else {
+            const uint4 va = *reinterpret_cast<const uint4*>(rec + h * 1024 + lane * 32);
+            const uint4 vb = *reinterpret_cast<const uint4*>(rec + h * 1024 + lane * 32 + 16);
+            const uint32_t rg[4] = {va.x, va.y, va.z, va.w};
+            const uint32_t rh[4] = {vb.x, vb.y, vb.z, vb.w};
+            const uint32_t X[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                uint32_t a[4];
+                unpack_w8_word(rg[jj], a[0], a[2]);
+                unpack_w8_word(rh[jj], a[1], a[3]);
+                mma_bf16_16816(part[h], a, X[2 * jj], X[2 * jj + 1]);
+            }
+        }
+    }
+    if constexpr (W4) {
+        // part[0] + part[1] hold sum (1032 + q) x (rows g) and
+        // sum (1152 + 16q) x (rows g+8) over the group's 128 columns
+        const float2 s2x = *reinterpret_cast<const float2*>(sx + grp * 8 + 2 * t);
+        const uint32_t sv = *reinterpret_cast<const uint32_t*>(rec + 1024 + 4 * g);
+        const __half2 s2 = *reinterpret_cast<const __half2*>(&sv);
+        const float s_lo = __low2float(s2), s_hi = __high2float(s2) * 0.0625f;
+        acc[0] = fmaf(fmaf(-1032.f, s2x.x, part[0][0] + part[1][0]), s_lo, acc[0]);
+        acc[2] = fmaf(fmaf(-1152.f, s2x.x, part[0][2] + part[1][2]), s_hi, acc[2]);
+        if constexpr (!M1) {
+            acc[1] = fmaf(fmaf(-1032.f, s2x.y, part[0][1] + part[1][1]), s_lo, acc[1]);
+            acc[3] = fmaf(fmaf(-1152.f, s2x.y, part[0][3] + part[1][3]), s_hi, acc[3]);
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            if (!M1 || !(e & 1)) acc[e] += part[0][e] + part[1][e];
+    }
+}
+
+// The `len` units of a stage (groups grp0.. of one row block): warp w takes
+// units w, w + 8, ... Stages of 16 or 32 units get a fixed trip count, which
+// lets the compiler overlap one unit's loads and unpack with the previous
+// unit's MMA chain.
+template <int FMT, bool M1>
+__device__ __forceinline__ void gemv_stage(const uint8_t* st, int len, const uint8_t* xrow_g, const float* sx,
+                                           int grp0, int warp, int lane, int g, int t, float (&acc)[4]) {
+    constexpr int UB = FMT == AMCU_WFMT_INT4 ? kW4PairBytes : 2048;
+    if (len == 4 * kGemvConsumers) {
+#pragma unroll
+        for (int uu = 0; uu < 4; ++uu) {
+            const int u = warp + uu * kGemvConsumers;
+            gemv_unit<FMT, M1>(st + u * UB, xrow_g, sx, grp0 + u, lane, g, t, acc);
+        }
+    } else if (len == 2 * kGemvConsumers) {
+#pragma unroll
+        for (int uu = 0; uu < 2; ++uu) {
+            const int u = warp + uu * kGemvConsumers;
+            gemv_unit<FMT, M1>(st + u * UB, xrow_g, sx, grp0 + u, lane, g, t, acc);
+        }
+    } else {
+        for (int u = warp; u < len; u += kGemvConsumers)
+            gemv_unit<FMT, M1>(st + u * UB, xrow_g, sx, grp0 + u, lane, g, t, acc);
+    }
+}
+
+template <int FMT, int EPI, bool M1>
 __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvParams p) {
     constexpr bool W4 = FMT == AMCU_WFMT_INT4;
     constexpr int UB = W4 ? kW4PairBytes : 2048;  // bytes per 128-column group unit
@@ -253,12 +349,12 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
     uint64_t* empty = full + S;
 
+    // row blocks rb0 .. rb0 + nr - 1, per_row stages of SU units each (SU divides G)
     const int nrb = (int)(p.n / 16);
     const int rb0 = blockIdx.x * p.rb_per_cta;
     const int nr = (rb0 + p.rb_per_cta < nrb ? rb0 + p.rb_per_cta : nrb) - rb0;
-    const int per_row = G / SU;  // stages per row block
+    const int per_row = G / SU;
     const int total = nr * per_row;
-    const uint8_t* run = static_cast<const uint8_t*>(p.w) + (size_t)rb0 * G * UB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -276,6 +372,7 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
         if (lane == 0) {
             int slot = 0;
             uint32_t phase = 0;
+            const uint8_t* run = static_cast<const uint8_t*>(p.w) + (size_t)rb0 * G * UB;
             for (int i = 0; i < total; ++i) {
                 if (i >= S && !mbar_wait(&empty[slot], phase ^ 1u)) {
                     record_device_error(p.err, kErrGemvEmptyWait);
@@ -315,81 +412,27 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
     bool ok = true;  // false once a wait ran out: keep the control flow, skip further waits
     int fail_i = -1;
     int par = 0;
-    for (int r = 0; r < nr; ++r, par ^= 1) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int j = 0; j < per_row; ++j) {
-            const int i = r * per_row + j;
-            if (ok && !mbar_wait(&full[slot], phase)) {
-                ok = false;
-                fail_i = i;
-                if (lane == 0) record_device_error(p.err, kErrGemvFullWait);
-            }
-            const uint8_t* st = ring + slot * SBY;
-            for (int u = warp; u < SU; u += kGemvConsumers) {  // this warp's group units of the stage
-                const int grp = j * SU + u;                       // group within the row block
-                const uint8_t* rec = st + u * UB;
-                const uint8_t* xp = xrow_g + grp * 256;
-                float part[2][4];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) part[h][e] = 0.f;
-                    const uint4 x0 = *reinterpret_cast<const uint4*>(xp + h * 128);
-                    const uint4 x1 = *reinterpret_cast<const uint4*>(xp + h * 128 + 16);
-                    if constexpr (W4) {
-                        const uint4 wv = *reinterpret_cast<const uint4*>(rec + h * 512 + lane * 16);
-                        uint32_t a[4];
-                        unpack_w4_word_f16(wv.x, a);
-                        mma_f16_16816(part[h], a, x0.x, x0.y);
-                        unpack_w4_word_f16(wv.y, a);
-                        mma_f16_16816(part[h], a, x0.z, x0.w);
-                        unpack_w4_word_f16(wv.z, a);
-                        mma_f16_16816(part[h], a, x1.x, x1.y);
-                        unpack_w4_word_f16(wv.w, a);
-                        mma_f16_16816(part[h], a, x1.z, x1.w);
-                    } else {
-                        const uint4 va = *reinterpret_cast<const uint4*>(rec + h * 1024 + lane * 32);
-                        const uint4 vb = *reinterpret_cast<const uint4*>(rec + h * 1024 + lane * 32 + 16);
-                        const uint32_t rg[4] = {va.x, va.y, va.z, va.w};
-                        const uint32_t rh[4] = {vb.x, vb.y, vb.z, vb.w};
-                        const uint32_t X[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-                        for (int jj = 0; jj < 4; ++jj) {
-                            uint32_t a[4];
-                            unpack_w8_word(rg[jj], a[0], a[2]);
-                            unpack_w8_word(rh[jj], a[1], a[3]);
-                            mma_bf16_16816(part[h], a, X[2 * jj], X[2 * jj + 1]);
-                        }
-                    }
-                }
-                if constexpr (W4) {
-                    // part[0] + part[1] hold sum (1032 + q) x (rows g) and
-                    // sum (1152 + 16q) x (rows g+8) over the group's 128 columns
-                    const float2 s2x = *reinterpret_cast<const float2*>(sx + grp * 8 + 2 * t);
-                    const uint32_t sv = *reinterpret_cast<const uint32_t*>(rec + 1024 + 4 * g);
-                    const __half2 s2 = *reinterpret_cast<const __half2*>(&sv);
-                    const float s_lo = __low2float(s2), s_hi = __high2float(s2) * 0.0625f;
-                    acc[0] = fmaf(fmaf(-1032.f, s2x.x, part[0][0] + part[1][0]), s_lo, acc[0]);
-                    acc[1] = fmaf(fmaf(-1032.f, s2x.y, part[0][1] + part[1][1]), s_lo, acc[1]);
-                    acc[2] = fmaf(fmaf(-1152.f, s2x.x, part[0][2] + part[1][2]), s_hi, acc[2]);
-                    acc[3] = fmaf(fmaf(-1152.f, s2x.y, part[0][3] + part[1][3]), s_hi, acc[3]);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) acc[e] += part[0][e] + part[1][e];
-                }
-            }
-            __syncwarp();  // every lane has read the stage
-            if (lane == 0) mbar_arrive(&empty[slot]);
-            if (++slot == S) {
-                slot = 0;
-                phase ^= 1;
-            }
+    float acc[4];
+    // one stage: wait for it, run its units, release it
+    auto stage = [&](int i, int grp0, int len) {
+        if (ok && !mbar_wait(&full[slot], phase)) {
+            ok = false;
+            fail_i = i;
+            if (lane == 0) record_device_error(p.err, kErrGemvFullWait);
         }
-        // row-block end: publish this warp's partial tile, meet the other
-        // warps, and let one warp reduce and apply the epilogue
+        gemv_stage<FMT, M1>(ring + slot * SBY, len, xrow_g, sx, grp0, warp, lane, g, t, acc);
+        __syncwarp();  // every lane has read the stage
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == S) {
+            slot = 0;
+            phase ^= 1;
+        }
+    };
+    // row-block end: publish this warp's partial tile, meet the other warps,
+    // and let one warp reduce and apply the epilogue
+    auto finish = [&](int rb) {
         red[(par * kGemvConsumers + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         named_bar_sync(1, NT);
-        const int rb = rb0 + r;
         if (warp == rb % kGemvConsumers) {
             float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
@@ -399,6 +442,12 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
             }
             gemv_epilogue<FMT, EPI>(p, rb, g, t, s4, rm0, rm1);
         }
+        par ^= 1;
+    };
+    for (int r = 0; r < nr; ++r) {
+        acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+        for (int j = 0; j < per_row; ++j) stage(r * per_row + j, j * SU, SU);
+        finish(rb0 + r);
     }
     if (fail_i >= 0 && warp == 0 && lane == 0) {
         // A wait ran out: stages fail_i .. total - 1 may still be landing.
@@ -458,10 +507,20 @@ __global__ void gemm_plain_kernel(GemvParams p) {
 }
 
 template <int FMT, int EPI>
+static void launch_gemv_variant(const GemvParams& q, int64_t grid, size_t smem, cudaStream_t s) {
+    constexpr int kMaxSmem = 224 * 1024;
+    auto go = [&](auto kern) {
+        set_func_attr_once((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+        launch_pdl(kern, dim3((unsigned)grid), dim3(kGemvThreads), smem, s, q);
+    };
+    if (q.m == 1) go(gemv_tc_kernel<FMT, EPI, true>);
+    else go(gemv_tc_kernel<FMT, EPI, false>);
+}
+
+template <int FMT, int EPI>
 static void launch_gemv_one(GemvParams p, cudaStream_t s) {
     constexpr int kMaxSmem = 224 * 1024;
     const int smem_sm = smem_per_sm();
-    set_func_attr_once((const void*)gemv_tc_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
     constexpr int UB = FMT == AMCU_WFMT_INT4 ? kW4PairBytes : 2048;
     const int per_cta2 = smem_sm / GEMV_CPS - 2048;  // GEMV_CPS CTAs per SM (room for the per-CTA reserve)
     const int per_cta1 = kMaxSmem;                  // one CTA per SM
@@ -512,8 +571,8 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
         q.x = static_cast<const __nv_bfloat16*>(p.x) + m0 * p.x_stride;
         q.y = static_cast<__nv_bfloat16*>(p.y) + m0 * p.y_stride;
         if (p.residual) q.residual = static_cast<const __nv_bfloat16*>(p.residual) + m0 * p.y_stride;
-        launch_pdl(gemv_tc_kernel<FMT, EPI>, dim3((unsigned)grid), dim3(kGemvThreads),
-                   (size_t)gemv_smem<FMT>((int)q.m, p.k, su * UB, stages).total, s, q);
+        const size_t smem = (size_t)gemv_smem<FMT>((int)q.m, p.k, su * UB, stages).total;
+        launch_gemv_variant<FMT, EPI>(q, grid, smem, s);
     }
 }
 

@@ -8,8 +8,10 @@
 // kv_head = q_head / (n_q / n_kv)).
 //
 // A CTA takes 64 query rows of one q head; each of its 4 warps owns 16 rows.
-// Key tiles of 64 rows go through shared memory (K row-major, V transposed,
-// both padded so the fragment loads hit distinct banks). Per tile a warp
+// Key tiles of 64 rows go through shared memory in two stages (cp.async: the
+// next tile loads while this one is used), K and V both row-major with rows
+// padded to 16 bytes apart modulo 128, so the ldmatrix fragment loads (K
+// plain, V transposed) hit distinct banks. Per tile a warp
 // computes S = Q K^T with mma.sync m16n8k16 (bf16 in, fp32 out), masks the
 // keys past each row's position, updates the running max / sum (online
 // softmax in base 2, fp32), and accumulates O += P V with P converted to bf16
@@ -47,26 +49,69 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+// 16-byte global -> shared copy; src_bytes 0 fills the 16 bytes with zeros
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int D>
+constexpr int fp_smem_bytes() { return 2 * 2 * kFpBN * (D + 8) * 2; }  // [K, V][2 stages][64 keys][D + 8]
+
 template <int D>
 __global__ void __launch_bounds__(kFpThreads) attn_prefill_flash_kernel(FpParams p) {
-    constexpr int KS = D / 16;       // k-steps of S = Q K^T
-    constexpr int DT = D / 8;        // n-tiles of O
-    constexpr int KST = D + 8;       // K row stride in shared memory (elements)
-    constexpr int VST = kFpBN + 8;   // V^T row stride
-    __shared__ __align__(16) __nv_bfloat16 Ks[kFpBN * KST];
-    __shared__ __align__(16) __nv_bfloat16 Vt[D * VST];
+    constexpr int KS = D / 16;     // k-steps of S = Q K^T
+    constexpr int DT = D / 8;      // n-tiles of O
+    constexpr int ST = D + 8;      // K / V row stride in shared memory (elements): 16 B apart mod 128 B,
+                                   // so the 8 rows of an ldmatrix hit distinct banks
+    constexpr int TILE = kFpBN * ST;
+    extern __shared__ __align__(16) __nv_bfloat16 fp_smem[];
+    __nv_bfloat16* Ks = fp_smem;              // [2][64][ST]
+    __nv_bfloat16* Vs = fp_smem + 2 * TILE;   // [2][64][ST]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int64_t b = blockIdx.z, h = blockIdx.y;
     const int64_t kvh = h / p.grp;
-    const int64_t i0 = (int64_t)blockIdx.x * kFpBM;
+    // the longest causal row blocks first (they need the most key tiles)
+    const int64_t i0 = (int64_t)(gridDim.x - 1 - blockIdx.x) * kFpBM;
     pdl_wait();
     pdl_trigger();
     const int64_t p0 = p.seq_pos[b];
     const int64_t last = (i0 + kFpBM < p.R ? i0 + kFpBM : p.R) - 1;  // last valid row of the CTA
     int64_t L = p0 + last + 1;                                       // keys this CTA needs
     if (L > p.capacity) L = p.capacity;
+
+    const __nv_bfloat16* kbase = p.kc + b * p.slot_stride + kvh * p.capacity * D;
+    const __nv_bfloat16* vbase = p.vc + b * p.slot_stride + kvh * p.capacity * D;
+    const int ntiles = (int)((L + kFpBN - 1) / kFpBN);
+    // keys k0 .. k0 + 63 of K and V into stage st (zeros past L)
+    auto load_tile = [&](int kt, int st) {
+        const int64_t k0 = (int64_t)kt * kFpBN;
+        for (int e = threadIdx.x; e < kFpBN * (D / 8); e += kFpThreads) {
+            const int kr = e / (D / 8), c8 = e % (D / 8);
+            const int64_t key = k0 + kr;
+            const bool in = key < L;
+            const int64_t off = (in ? key : 0) * D + c8 * 8;
+            cp_async16(Ks + st * TILE + kr * ST + c8 * 8, kbase + off, in ? 16u : 0u);
+            cp_async16(Vs + st * TILE + kr * ST + c8 * 8, vbase + off, in ? 16u : 0u);
+        }
+        cp_async_commit();
+    };
+    if (ntiles > 0) load_tile(0, 0);
 
     // this lane's two rows (g and g+8 of the warp's 16) and their positions
     const int64_t ra = i0 + warp * 16 + g, rb = ra + 8;
@@ -86,36 +131,34 @@ __global__ void __launch_bounds__(kFpThreads) attn_prefill_flash_kernel(FpParams
     for (int i = 0; i < DT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float ma = -INFINITY, mb = -INFINITY, la = 0.f, lb = 0.f;
 
-    const __nv_bfloat16* kbase = p.kc + b * p.slot_stride + kvh * p.capacity * D;
-    const __nv_bfloat16* vbase = p.vc + b * p.slot_stride + kvh * p.capacity * D;
-    const int ntiles = (int)((L + kFpBN - 1) / kFpBN);
+    // ldmatrix lane roles: lane l addresses row l % 8 of matrix l / 8
+    const int lm = lane >> 3, lr = lane & 7;
     for (int kt = 0; kt < ntiles; ++kt) {
-        const int64_t k0 = (int64_t)kt * kFpBN;
-        __syncthreads();  // the previous tile is no longer read
-        // ---- stage keys k0 .. k0 + 63 (zeros past L)
-        for (int e = threadIdx.x; e < kFpBN * (D / 8); e += kFpThreads) {
-            const int kr = e / (D / 8), c8 = e % (D / 8);
-            const int64_t key = k0 + kr;
-            uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-            if (key < L) {
-                kv = *reinterpret_cast<const uint4*>(kbase + key * D + c8 * 8);
-                vv = *reinterpret_cast<const uint4*>(vbase + key * D + c8 * 8);
-            }
-            *reinterpret_cast<uint4*>(Ks + kr * KST + c8 * 8) = kv;
-            const __nv_bfloat16* ve = reinterpret_cast<const __nv_bfloat16*>(&vv);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) Vt[(c8 * 8 + j) * VST + kr] = ve[j];
+        const int st = kt & 1;
+        if (kt + 1 < ntiles) {
+            load_tile(kt + 1, st ^ 1);  // that stage was last read in iteration kt - 1
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
-        __syncthreads();
-        // ---- S = Q K^T for this warp's 16 rows x 64 keys
+        __syncthreads();  // tile kt is in shared memory for every thread
+        const __nv_bfloat16* Kt = Ks + st * TILE;
+        const __nv_bfloat16* Vt = Vs + st * TILE;
+        const int64_t k0 = (int64_t)kt * kFpBN;
+        // ---- S = Q K^T for this warp's 16 rows x 64 keys. B[k = d][n = key] =
+        // K[key][d]: one ldmatrix.x4 gives n-tile nt's fragments of k-steps
+        // ks and ks + 1 (matrices: d 16ks, 16ks+8, 16ks+16, 16ks+24)
         float s[8][4];
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
             s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-            const __nv_bfloat16* krow = Ks + (nt * 8 + g) * KST + 2 * t;
 #pragma unroll
-            for (int ks = 0; ks < KS; ++ks)
-                mma_bf16_16816(s[nt], qf[ks], ld_b32(krow + 16 * ks), ld_b32(krow + 16 * ks + 8));
+            for (int ks = 0; ks < KS; ks += 2) {
+                uint32_t kf[4];
+                ldsm_x4(kf, Kt + (nt * 8 + lr) * ST + 16 * ks + 8 * lm);
+                mma_bf16_16816(s[nt], qf[ks], kf[0], kf[1]);
+                mma_bf16_16816(s[nt], qf[ks + 1], kf[2], kf[3]);
+            }
         }
         // ---- causal mask, scale, running max
         float mxa = -INFINITY, mxb = -INFINITY;
@@ -158,18 +201,23 @@ __global__ void __launch_bounds__(kFpThreads) attn_prefill_flash_kernel(FpParams
             la += s[nt][0] + s[nt][1];
             lb += s[nt][2] + s[nt][3];
         }
-        // ---- O += P V, k-step kk covers keys 16 kk .. +15 (n-tiles 2kk, 2kk+1 of S)
+        // ---- O += P V, k-step kk covers keys 16 kk .. +15 (n-tiles 2kk, 2kk+1
+        // of S). B[k = key][n = d] = V[key][d]: one ldmatrix.x4.trans gives the
+        // fragments of d-tiles dt and dt + 1 (matrices: keys +0 / +8 x d 8dt / 8dt+8)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
             const uint32_t pf[4] = {pack_bf16(s[2 * kk][0], s[2 * kk][1]), pack_bf16(s[2 * kk][2], s[2 * kk][3]),
                                     pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]),
                                     pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3])};
 #pragma unroll
-            for (int dt = 0; dt < DT; ++dt) {
-                const __nv_bfloat16* vrow = Vt + (dt * 8 + g) * VST + kk * 16 + 2 * t;
-                mma_bf16_16816(o[dt], pf, ld_b32(vrow), ld_b32(vrow + 8));
+            for (int dt = 0; dt < DT; dt += 2) {
+                uint32_t vf[4];
+                ldsm_x4_trans(vf, Vt + (kk * 16 + 8 * (lm & 1) + lr) * ST + 8 * (dt + (lm >> 1)));
+                mma_bf16_16816(o[dt], pf, vf[0], vf[1]);
+                mma_bf16_16816(o[dt + 1], pf, vf[2], vf[3]);
             }
         }
+        __syncthreads();  // every warp is done with stage st before it is refilled
     }
     // ---- normalise and store
     la += __shfl_xor_sync(0xffffffffu, la, 1);
@@ -199,6 +247,8 @@ bool launch_attn_prefill_flash(const AmcuAttentionArgs* a, cudaStream_t s) {
     const int64_t qs = a->q_stride ? a->q_stride : a->n_q_heads * a->head_dim;
     const int64_t os = a->out_stride ? a->out_stride : a->n_q_heads * a->head_dim;
     if (qs % 2 != 0 || os % 2 != 0 || !aligned(a->out, 4)) return false;
+    const int64_t slot = a->slot_stride ? a->slot_stride : a->n_kv_heads * a->capacity * a->head_dim;
+    if (!aligned(a->k_cache, 16) || !aligned(a->v_cache, 16) || slot % 8 != 0) return false;  // 16-byte copies
     FpParams p{};
     p.q = static_cast<const __nv_bfloat16*>(a->q);
     p.q_stride = qs;
@@ -214,8 +264,15 @@ bool launch_attn_prefill_flash(const AmcuAttentionArgs* a, cudaStream_t s) {
     p.grp = (int)(a->n_q_heads / a->n_kv_heads);
     p.scale_log2 = (float)(1.0 / sqrt((double)a->head_dim)) * kFpLog2e;
     const dim3 grid((unsigned)((p.R + kFpBM - 1) / kFpBM), (unsigned)a->n_q_heads, (unsigned)(a->rows / p.R));
-    if (a->head_dim == 128) launch_pdl(attn_prefill_flash_kernel<128>, grid, dim3(kFpThreads), 0, s, p);
-    else launch_pdl(attn_prefill_flash_kernel<64>, grid, dim3(kFpThreads), 0, s, p);
+    if (a->head_dim == 128) {
+        set_func_attr_once((const void*)attn_prefill_flash_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           fp_smem_bytes<128>());
+        launch_pdl(attn_prefill_flash_kernel<128>, grid, dim3(kFpThreads), fp_smem_bytes<128>(), s, p);
+    } else {
+        set_func_attr_once((const void*)attn_prefill_flash_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           fp_smem_bytes<64>());
+        launch_pdl(attn_prefill_flash_kernel<64>, grid, dim3(kFpThreads), fp_smem_bytes<64>(), s, p);
+    }
     return true;
 }
 

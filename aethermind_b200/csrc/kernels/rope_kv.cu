@@ -23,50 +23,78 @@ __global__ void rope_table_kernel(double theta, int64_t d, int64_t max_pos, floa
     }
 }
 
-// One CTA per (row, head); heads [0, nq) are query heads (rotated in place),
-// [nq, nq + nkv) key heads (rotated into the cache), the last nkv value
-// heads (copied into the cache). Thread i handles the pair (i, i + d/2).
+// One CTA per row; its threads walk the work items of all heads: heads
+// [0, nq) are query heads (rotated in place), [nq, nq + nkv) key heads
+// (rotated into the cache), the last nkv value heads (copied into the cache).
+// A rotation item is two adjacent pairs (i, i + d/2), (i + 1, i + 1 + d/2),
+// loaded and stored as two-element vectors; a value item is two elements.
 template <typename T>
-__global__ void __launch_bounds__(64) rope_kv_kernel(AmcuRopeKvArgs a) {
+struct Pair2;
+template <>
+struct Pair2<float> {
+    using V = float2;
+    static __device__ __forceinline__ void get(const V& v, float& a, float& b) { a = v.x; b = v.y; }
+    static __device__ __forceinline__ V make(float a, float b) { return make_float2(a, b); }
+};
+template <>
+struct Pair2<__nv_bfloat16> {
+    using V = __nv_bfloat162;
+    static __device__ __forceinline__ void get(const V& v, float& a, float& b) {
+        a = __low2float(v);
+        b = __high2float(v);
+    }
+    static __device__ __forceinline__ V make(float a, float b) { return __floats2bfloat162_rn(a, b); }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) rope_kv_kernel(AmcuRopeKvArgs a) {
+    using P2 = Pair2<T>;
+    using V = typename P2::V;
     pdl_wait();
     pdl_trigger();
     const int64_t row = blockIdx.x;
-    const int64_t head = blockIdx.y;
     const int64_t b = row / a.rows_per_seq;
     const int64_t pos = (int64_t)a.seq_pos[b] + row % a.rows_per_seq;
-    const int64_t d = a.head_dim, half = d / 2;
+    const int64_t d = a.head_dim, half = d / 2, hp = half / 2;  // hp rotation items per head
     if (pos < 0 || pos >= a.capacity) {
-        if (a.status && threadIdx.x == 0 && head == 0) atomicExch(a.status, (int32_t)AM_STATUS_OUT_OF_RANGE);
+        if (a.status && threadIdx.x == 0) atomicExch(a.status, (int32_t)AM_STATUS_OUT_OF_RANGE);
         return;
     }
     const int64_t slot_stride = a.slot_stride ? a.slot_stride : a.n_kv_heads * a.capacity * d;
     const int64_t nq = a.n_q_heads, nkv = a.n_kv_heads;
-    if (head >= nq + nkv) {  // value head: copy
-        const int64_t h = head - nq - nkv;
-        const T* v = static_cast<const T*>(a.v) + row * a.v_stride + h * d;
-        T* vc = static_cast<T*>(a.v_cache) + b * slot_stride + (h * a.capacity + pos) * d;
-        for (int64_t i = threadIdx.x; i < d; i += blockDim.x) vc[i] = v[i];
-        return;
-    }
-    for (int64_t i = threadIdx.x; i < half; i += blockDim.x) {
-        float c, s;
-        if (a.cos_sin) {
-            const float2 v = reinterpret_cast<const float2*>(a.cos_sin)[pos * half + i];
-            c = v.x;
-            s = v.y;
-        } else {
-            rope_angle(a.theta, d, pos, i, c, s);
+    const int64_t rot_items = (nq + nkv) * hp, items = rot_items + nkv * (d / 2);
+    for (int64_t e = threadIdx.x; e < items; e += blockDim.x) {
+        if (e >= rot_items) {  // value head: copy two elements
+            const int64_t f = e - rot_items, h = f / (d / 2), c = 2 * (f % (d / 2));
+            const V v = *reinterpret_cast<const V*>(static_cast<const T*>(a.v) + row * a.v_stride + h * d + c);
+            *reinterpret_cast<V*>(static_cast<T*>(a.v_cache) + b * slot_stride + (h * a.capacity + pos) * d + c) = v;
+            continue;
         }
+        const int64_t head = e / hp, i = 2 * (e % hp);
         const bool is_q = head < nq;
         const T* src = is_q ? static_cast<const T*>(a.q) + row * a.q_stride + head * d
                             : static_cast<const T*>(a.k) + row * a.k_stride + (head - nq) * d;
-        const float x1 = Act<T>::load(src[i]), x2 = Act<T>::load(src[i + half]);
-        const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-        const float o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+        float x1[2], x2[2];
+        P2::get(*reinterpret_cast<const V*>(src + i), x1[0], x1[1]);
+        P2::get(*reinterpret_cast<const V*>(src + i + half), x2[0], x2[1]);
+        float o1[2], o2[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            float c, sn;
+            if (a.cos_sin) {
+                const float2 cs = reinterpret_cast<const float2*>(a.cos_sin)[pos * half + i + j];
+                c = cs.x;
+                sn = cs.y;
+            } else {
+                rope_angle(a.theta, d, pos, i + j, c, sn);
+            }
+            o1[j] = __fsub_rn(__fmul_rn(x1[j], c), __fmul_rn(x2[j], sn));
+            o2[j] = __fadd_rn(__fmul_rn(x2[j], c), __fmul_rn(x1[j], sn));
+        }
         T* dst = is_q ? static_cast<T*>(a.q) + row * a.q_stride + head * d
                       : static_cast<T*>(a.k_cache) + b * slot_stride + ((head - nq) * a.capacity + pos) * d;
-        dst[i] = Act<T>::store(o1);
-        dst[i + half] = Act<T>::store(o2);
+        *reinterpret_cast<V*>(dst + i) = P2::make(o1[0], o1[1]);
+        *reinterpret_cast<V*>(dst + i + half) = P2::make(o2[0], o2[1]);
     }
 }
 
@@ -86,11 +114,20 @@ extern "C" am_status_code amcu_rope_kv_write(const AmcuRopeKvArgs* a, void* stre
     AMCU_REQUIRE(a->rows_per_seq > 0, "amcu_rope_kv_write: rows_per_seq must be positive");
     AMCU_REQUIRE(a->capacity > 0, "amcu_rope_kv_write: capacity must be positive");
     AMCU_REQUIRE(a->theta > 0.0, "amcu_rope_kv_write: theta must be positive");
-    const dim3 grid((unsigned)a->rows, (unsigned)(a->n_q_heads + 2 * a->n_kv_heads));
+    AMCU_REQUIRE(a->head_dim % 4 == 0, "amcu_rope_kv_write: head_dim must be a multiple of 4");
+    {
+        const int64_t es = a->dtype == AMCU_F32 ? 8 : 4;  // bytes of a two-element vector
+        const int64_t qs = a->q_stride, ks = a->k_stride, vs = a->v_stride;
+        AMCU_REQUIRE(aligned(a->q, es) && aligned(a->k, es) && aligned(a->v, es) && aligned(a->k_cache, es) &&
+                             aligned(a->v_cache, es) && qs % 2 == 0 && ks % 2 == 0 && vs % 2 == 0 &&
+                             a->slot_stride % 2 == 0,
+                     "amcu_rope_kv_write: rows must start on two-element boundaries");
+    }
+    const dim3 grid((unsigned)a->rows);
     if (a->dtype == AMCU_F32)
-        launch_pdl(rope_kv_kernel<float>, grid, dim3(64), 0, as_stream(stream), *a);
+        launch_pdl(rope_kv_kernel<float>, grid, dim3(256), 0, as_stream(stream), *a);
     else if (a->dtype == AMCU_BF16)
-        launch_pdl(rope_kv_kernel<__nv_bfloat16>, grid, dim3(64), 0, as_stream(stream), *a);
+        launch_pdl(rope_kv_kernel<__nv_bfloat16>, grid, dim3(256), 0, as_stream(stream), *a);
     else
         return set_error(AM_STATUS_INVALID_ARGUMENT, "amcu_rope_kv_write: dtype must be f32 or bf16");
     return check_launch("amcu_rope_kv_write");

@@ -247,8 +247,14 @@ def attention_rope_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_c
     """Fused decode step (amcu_attn_decode_rope): RoPE, KV-cache append and
     attention for one row per sequence. q is not modified."""
     _require_cuda(q, k, v, k_cache, v_cache, seq_pos)
+    o = out if out is not None else torch.empty(q.shape[0], n_q * head_dim, dtype=q.dtype, device=q.device)
+    r, a = _rope_attn_args(q, k, v, k_cache, v_cache, seq_pos, n_q, n_kv, head_dim, theta, cos_sin, status, o)
+    check(lib().amcu_attn_decode_rope(C.byref(r), C.byref(a), _stream()), "amcu_attn_decode_rope")
+    return o
+
+
+def _rope_attn_args(q, k, v, k_cache, v_cache, seq_pos, n_q, n_kv, head_dim, theta, cos_sin, status, o):
     rows = q.shape[0]
-    o = out if out is not None else torch.empty(rows, n_q * head_dim, dtype=q.dtype, device=q.device)
     r = L.AmcuRopeKvArgs()
     r.q, r.k, r.v = _p(q), _p(k), _p(v)
     r.q_stride, r.k_stride, r.v_stride = q.stride(0), k.stride(0), v.stride(0)
@@ -271,8 +277,7 @@ def attention_rope_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_c
     a.n_q_heads, a.n_kv_heads, a.head_dim = n_q, n_kv, head_dim
     a.dtype = _dt(q)
     a.max_context = k_cache.shape[2]
-    check(lib().amcu_attn_decode_rope(C.byref(r), C.byref(a), _stream()), "amcu_attn_decode_rope")
-    return o
+    return r, a
 
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

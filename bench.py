@@ -106,11 +106,17 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.rows)}
 
 
+# (n, k) of the 8B decode GEMVs (q/k/v fused, o, gate/up interleaved, down, lm_head)
+GEMV_SHAPES_8B = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (2 * 14336, 4096), "down": (4096, 14336),
+                  "lm_head": (128256, 4096)}
+
+
 def gemv_roofline(hbm_peak: float, ncopy: int | None = None, reps: int | None = None, m: int = 1,
                   shape: str = "gate_up") -> dict:
-    """Times the W4 GEMV of the 8B gate/up projection (N = 2 x 14336, K = 4096;
-    shape "down": N = 4096, K = 14336) alone for m activation rows, rotating
-    over enough weight copies that every launch reads HBM."""
+    """Times one W4 GEMV of the 8B decode step (GEMV_SHAPES_8B; the bench's
+    roofline line uses gate/up, N = 2 x 14336, K = 4096) alone for m
+    activation rows, rotating over enough weight copies that every launch
+    reads HBM."""
     import ctypes as C
 
     import torch
@@ -118,7 +124,7 @@ def gemv_roofline(hbm_peak: float, ncopy: int | None = None, reps: int | None = 
     from aethermind_b200 import _lib as L
     from aethermind_b200 import ops
 
-    n, k = (2 * 14336, 4096) if shape == "gate_up" else (4096, 14336)
+    n, k = GEMV_SHAPES_8B[shape]
     q, s = ops.synth_w4(SEED, 99, n, k, 0.004)
     copies = []
     per = n * k // 2 + n * (k // 128) * 2
@@ -198,7 +204,7 @@ def op_bench(args) -> None:
     import torch
     torch.cuda.set_device(0)
     hbm_peak, tc_peak, _ = _peaks()
-    if args.op in ("gemv_gate_up", "gemv_down"):
+    if args.op.startswith("gemv_") and args.op[5:] in GEMV_SHAPES_8B:
         r = gemv_roofline(hbm_peak, ncopy=args.copies, reps=args.reps, m=args.m, shape=args.op[5:])
     elif args.op == "gemm_gate_up":
         r = gemm_prefill_timing(tc_peak, reps=args.reps or 20)
@@ -347,7 +353,7 @@ def main() -> None:
     ap.add_argument("--decode", default="per-op", choices=["per-op", "persistent"],
                     help="decode plan: one kernel per op, or the persistent all-layers kernel (batch 1)")
     ap.add_argument("--nccl-allreduce", action="store_true", help="TP: NCCL for every all-reduce (no peer-memory one-shot)")
-    ap.add_argument("--op", default=None, help="time one kernel instead: gemv_gate_up | gemv_down | gemm_gate_up")
+    ap.add_argument("--op", default=None, help="time one kernel instead: gemv_{qkv,o,gate_up,down,lm_head} | gemm_gate_up")
     ap.add_argument("--copies", type=int, default=None, help="--op gemv_*: weight copies rotated")
     ap.add_argument("--m", type=int, default=1, help="--op gemv_*: activation rows")
     ap.add_argument("--reps", type=int, default=None, help="--op: timed launches")

@@ -180,7 +180,7 @@ def gemm_prefill_timing(tc_peak: float, reps: int = 20) -> dict:
     pw = ops.prepack_gate_up(L.WFMT_INT4, gq, gs, uq, us_, inter, k)
     x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
     y = torch.empty(m, inter, device="cuda", dtype=torch.bfloat16)
-    a, _, _ = ops._linear_args(x, pw, L.EPI_SILU_MUL, None, y)
+    a, _, ws = ops._linear_args(x, pw, L.EPI_SILU_MUL, None, y)  # ws: the tail split-K workspace, kept alive
     lib = L.lib()
     stream = torch.cuda.current_stream().cuda_stream
     for _ in range(3):
@@ -193,6 +193,7 @@ def gemm_prefill_timing(tc_peak: float, reps: int = 20) -> dict:
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / reps
+    del ws
     tflops = 2.0 * m * 2 * inter * k / (us * 1e-6) / 1e12
     return {"kernel": "gemm_w4_swap_kernel<SILU_MUL> (8B gate_up, m=512 n=28672 k=4096)", "bound": "tensor",
             "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s", "frac": round(tflops / tc_peak, 3),

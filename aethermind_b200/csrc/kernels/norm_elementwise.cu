@@ -50,6 +50,73 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ in, 
     }
 }
 
+// bf16 rows of at most 8 * 256 * CH elements (hidden % 8 == 0, 16-byte
+// aligned rows): 16-byte loads, the row kept in registers between the sum of
+// squares and the scaling; per element the same arithmetic as rmsnorm_kernel.
+template <int CH>
+__global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const __nv_bfloat16* __restrict__ in,
+                                                               const __nv_bfloat16* __restrict__ w,
+                                                               __nv_bfloat16* __restrict__ out,
+                                                               const __nv_bfloat16* __restrict__ res,
+                                                               __nv_bfloat16* res_out, int64_t hidden, int64_t in_stride,
+                                                               int64_t out_stride, float eps) {
+    pdl_wait();
+    pdl_trigger();
+    const int64_t row = blockIdx.x;
+    const int nch = (int)(hidden / 8);
+    const __nv_bfloat16* x = in + row * in_stride;
+    float v[CH][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int j = threadIdx.x + c * blockDim.x;
+        if (j >= nch) continue;
+        uint4 u = ld_u4(x + j * 8);
+        const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&u);
+        if (res) {
+            uint4 ru = ld_u4(res + row * in_stride + j * 8);
+            const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&ru);
+            uint4 o;
+            __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                v[c][e] = Act<__nv_bfloat16>::round(__bfloat162float(xe[e]) + __bfloat162float(re[e]));
+                oe[e] = __float2bfloat16_rn(v[c][e]);
+            }
+            *reinterpret_cast<uint4*>(res_out + row * in_stride + j * 8) = o;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[c][e] = __bfloat162float(xe[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += v[c][e] * v[c][e];
+    }
+    __shared__ float red[32];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = 1.0f / sqrtf(red[0] / (float)hidden + eps);
+    __nv_bfloat16* y = out + row * out_stride;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+        const int j = threadIdx.x + c * blockDim.x;
+        if (j >= nch) continue;
+        uint4 wu = ld_u4(w + j * 8);
+        const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wu);
+        uint4 o;
+        __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) oe[e] = __float2bfloat16_rn(v[c][e] * inv * __bfloat162float(we[e]));
+        *reinterpret_cast<uint4*>(y + j * 8) = o;
+    }
+}
+
 template <typename T>
 __global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ o, int64_t n) {
     pdl_wait();
@@ -325,6 +392,12 @@ am_status_code amcu_rmsnorm(const AmcuRmsNormArgs* a, void* stream) {
         launch_pdl(rmsnorm_kernel<float>, dim3((unsigned)a->rows), dim3(threads), 0, as_stream(stream), 
                 (const float*)a->input, (const float*)a->weight, (float*)a->output, (const float*)a->residual,
                 (float*)a->residual_out, a->hidden, is, os, a->eps);
+    else if (a->hidden % 8 == 0 && a->hidden <= 8 * 256 * 4 && is % 8 == 0 && os % 8 == 0 &&
+             aligned(a->input, 16) && aligned(a->weight, 16) && aligned(a->output, 16) &&
+             (!a->residual || (aligned(a->residual, 16) && aligned(a->residual_out, 16))))
+        launch_pdl(rmsnorm_bf16_vec_kernel<4>, dim3((unsigned)a->rows), dim3(256), 0, as_stream(stream),
+                   (const __nv_bfloat16*)a->input, (const __nv_bfloat16*)a->weight, (__nv_bfloat16*)a->output,
+                   (const __nv_bfloat16*)a->residual, (__nv_bfloat16*)a->residual_out, a->hidden, is, os, a->eps);
     else
         launch_pdl(rmsnorm_kernel<__nv_bfloat16>, dim3((unsigned)a->rows), dim3(threads), 0, as_stream(stream), 
                 (const __nv_bfloat16*)a->input, (const __nv_bfloat16*)a->weight, (__nv_bfloat16*)a->output,

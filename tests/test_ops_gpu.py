@@ -129,6 +129,25 @@ def test_rmsnorm_bf16_fused_residual(ops, orc, m):
     np.testing.assert_allclose(to_np(y), orc.rmsnorm(h_ref, w, 1e-5, bf=True), rtol=BF_RTOL, atol=BF_ATOL)
 
 
+@pytest.mark.parametrize("hidden", [2048, 8192, 4100, 16384])
+@pytest.mark.parametrize("with_res", [False, True])
+def test_rmsnorm_bf16_widths(ops, orc, hidden, with_res):
+    """bf16 rows that take the 16-byte-vector kernel (hidden % 8 == 0 and at
+    most 8192) and rows that keep the scalar one (4100, 16384)."""
+    m = 3
+    rng = np.random.default_rng(hidden)
+    x = orc.bf16_round(rng.normal(0, 2, (m, hidden)).astype(np.float32))
+    w = orc.bf16_round(rng.uniform(0.5, 1.5, hidden).astype(np.float32))
+    if with_res:
+        r = orc.bf16_round(rng.normal(0, 1, (m, hidden)).astype(np.float32))
+        y, h = ops.rmsnorm(bf16_dev(x), bf16_dev(w), 1e-5, residual=bf16_dev(r))
+        x = orc.bf16_round(x + r)
+        np.testing.assert_array_equal(to_np(h), x)
+    else:
+        y = ops.rmsnorm(bf16_dev(x), bf16_dev(w), 1e-5)
+    np.testing.assert_allclose(to_np(y), orc.rmsnorm(x, w, 1e-5, bf=True), rtol=BF_RTOL, atol=BF_ATOL)
+
+
 def test_rmsnorm_empty_rows_is_ok(ops):
     x = torch.empty(0, 64, device="cuda", dtype=torch.float32)
     y = ops.rmsnorm(x, torch.ones(64, device="cuda"), 1e-5)

@@ -24,6 +24,8 @@
 // Gate/up fusion: rows 0-7 of every tile are gate rows 8*rb..8*rb+7 and rows
 // 8-15 the matching up rows, so one lane holds gate and up of the same output
 // and the SiLU-Mul epilogue needs no data exchange.
+#include <cooperative_groups.h>
+
 #include "../amcu_internal.h"
 #include "allreduce.cuh"
 #include "common.cuh"
@@ -31,6 +33,8 @@
 #include "gemv_core.cuh"
 #include "gemv_stage.cuh"
 #include "mma_int4.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace amcu {
 
@@ -198,6 +202,172 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
     }
 }
 
+// K split over a 2-CTA thread-block cluster, for activation rows too long to
+// stage whole in one CTA (e.g. 8 rows of K = 14336: 229 KB of fp16). Cluster
+// c owns row blocks [c * rb_per_cta, ...); CTA rank r of the cluster stages
+// columns [r K/2, (r + 1) K/2) of every activation row and streams the
+// matching half of each row block's groups, with the same unit, stage and
+// staging code as gemv_tc_kernel. At a row block's end rank 1's reducing warp
+// stores its partial tile (already multiplied by its rows' overflow-guard
+// factors) into rank 0's shared memory and arrives on a rank-0 mbarrier (one
+// per row block of the cluster, used once); rank 0's warp waits for it
+// (bounded), adds the halves in rank order and applies the epilogue. The
+// weight is streamed once, where row slices would stream it once per slice.
+constexpr int kKs2MaxRb = 16;  // row blocks per cluster at most (partial slots)
+constexpr int32_t kErrGemvClusterWait = 0x104;
+
+__device__ __forceinline__ bool mbar_wait_acq_cluster(uint64_t* bar, uint32_t parity) {
+    const long long t0 = clock64();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+                "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+                " selp.u32 %0, 1, 0, p;\n}"
+                : "=r"(ok)
+                : "r"(smem_u32(bar)), "r"(parity)
+                : "memory");
+        if (ok) return true;
+        if (clock64() - t0 > kSpinLimitCycles) return false;
+    }
+}
+
+template <int FMT, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreads, 1) gemv_ks2_kernel(GemvParams p) {
+    constexpr bool W4 = FMT == AMCU_WFMT_INT4;
+    constexpr int UB = W4 ? kW4PairBytes : 2048;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int S = p.stages, SU = p.stage_units;
+    const int SBY = SU * UB;
+    const int G = (int)(p.k / 128), GH = G / 2;  // groups of a row block; of this CTA's half
+    const int64_t kh = (int64_t)GH * 128;
+    const int M = (int)p.m;
+    const int xrow = (int)(kh * 2 + kXPad);
+    const GemvSmem L = gemv_smem<FMT>(M, kh, SBY, S);
+    float4* red = reinterpret_cast<float4*>(smem + L.red);
+    float* sx = reinterpret_cast<float*>(smem + L.sx);
+    uint8_t* xs = smem + L.xs;
+    uint8_t* ring = smem + L.ring;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+    uint64_t* empty = full + S;
+    __shared__ __align__(16) float4 peer_part[kKs2MaxRb][32];  // rank 0: rank 1's partial per row block
+    __shared__ __align__(8) uint64_t peer_bar[kKs2MaxRb];
+
+    const int nrb = (int)(p.n / 16);
+    const int rb0 = (int)(blockIdx.x / 2) * p.rb_per_cta;
+    const int nr = (rb0 + p.rb_per_cta < nrb ? rb0 + p.rb_per_cta : nrb) - rb0;
+    const int per_row = GH / SU;
+    const int total = nr * per_row;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kGemvConsumers);
+        }
+        for (int r = 0; r < kKs2MaxRb; ++r) mbar_init(&peer_bar[r], 1);
+        fence_mbar_init();
+        l2_prefetch_share(p.l2_next);
+    }
+    cluster.sync();  // rank 0's barriers exist before rank 1 can arrive on them
+
+    if (warp == kGemvConsumers) {
+        if (lane == 0) {
+            int slot = 0;
+            uint32_t phase = 0;
+            for (int i = 0; i < total; ++i) {
+                if (i >= S && !mbar_wait(&empty[slot], phase ^ 1u)) {
+                    record_device_error(p.err, kErrGemvEmptyWait);
+                    break;
+                }
+                const int r = i / per_row, j = i - r * per_row;
+                const uint8_t* src = static_cast<const uint8_t*>(p.w) +
+                                     ((size_t)(rb0 + r) * G + (size_t)rank * GH + (size_t)j * SU) * UB;
+                mbar_expect_tx(&full[slot], SBY);
+                bulk_g2s(ring + slot * SBY, src, SBY, &full[slot]);
+                if (++slot == S) {
+                    slot = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+    } else {
+        pdl_wait();
+        pdl_trigger();
+        __shared__ StageShared stsh;
+        {
+            StageCtx sc{static_cast<const __nv_bfloat16*>(p.x) + (int64_t)rank * kh, p.x_stride, kh, M, nullptr,
+                        p.eps, xs, xrow, sx, &stsh, (int)threadIdx.x, kGemvConsumers * 32, 2};
+            stage_activations<W4>(sc);
+        }
+        const float rm0 = 2 * t < M ? stsh.row_mul[2 * t] : 1.f, rm1 = 2 * t + 1 < M ? stsh.row_mul[2 * t + 1] : 1.f;
+        const uint8_t* xrow_g = xs + (g < M ? g : 0) * xrow + 32 * t;
+        float4* peer0 = cluster.map_shared_rank(&peer_part[0][0], 0);  // rank 0's slots
+        uint32_t peer_bar0 = 0;  // shared::cluster address of rank 0's barrier 0
+        asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(peer_bar0) : "r"(smem_u32(&peer_bar[0])));
+        int slot = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        int fail_i = -1, par = 0;
+        float acc[4];
+        for (int r = 0; r < nr; ++r) {
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+            for (int j = 0; j < per_row; ++j) {
+                const int i = r * per_row + j;
+                if (ok && !mbar_wait(&full[slot], phase)) {
+                    ok = false;
+                    fail_i = i;
+                    if (lane == 0) record_device_error(p.err, kErrGemvFullWait);
+                }
+                gemv_stage<FMT, false>(ring + slot * SBY, SU, xrow_g, sx, j * SU, warp, lane, g, t, acc);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+                if (++slot == S) {
+                    slot = 0;
+                    phase ^= 1;
+                }
+            }
+            red[(par * kGemvConsumers + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            named_bar_sync(1, kGemvConsumers * 32);
+            if (warp == r % kGemvConsumers) {
+                float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int w = 0; w < kGemvConsumers; ++w) {
+                    const float4 v = red[(par * kGemvConsumers + w) * 32 + lane];
+                    s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
+                }
+                // this half's rows at their true scale (the guards may differ per half)
+                s4.x *= rm0; s4.y *= rm1; s4.z *= rm0; s4.w *= rm1;
+                if (rank == 1) {
+                    peer0[r * 32 + lane] = s4;
+                    __syncwarp();  // the warp's stores precede lane 0's release
+                    if (lane == 0)
+                        asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                                             peer_bar0 + (uint32_t)(r * sizeof(uint64_t)))
+                                     : "memory");
+                } else {
+                    if (!mbar_wait_acq_cluster(&peer_bar[r], 0)) {
+                        if (lane == 0) record_device_error(p.err, kErrGemvClusterWait);
+                    }
+                    const float4 o = peer_part[r][lane];
+                    s4.x += o.x; s4.y += o.y; s4.z += o.z; s4.w += o.w;
+                    gemv_epilogue<FMT, EPI>(p, rb0 + r, g, t, s4, 1.f, 1.f);
+                }
+            }
+            par ^= 1;
+        }
+        if (fail_i >= 0 && warp == 0 && lane == 0)
+            for (int k = fail_i; k < total; ++k)
+                if (!mbar_wait(&full[k % S], (uint32_t)(k / S) & 1u)) {
+                    record_device_error(p.err, kErrGemvDrain);
+                    break;
+                }
+    }
+    cluster.sync();  // rank 1's stores into rank 0 are done before either CTA leaves
+}
+
 template <int FMT>
 static int stage_units(int64_t k, int cap_w4 = 0) {
     // group units per stage: the largest divisor of k/128 up to a cap (INT4:
@@ -255,6 +425,43 @@ static void launch_gemv_variant(const GemvParams& q, int64_t grid, size_t smem, 
     else go(gemv_tc_kernel<FMT, EPI, false>);
 }
 
+// The 2-CTA K split (gemv_ks2_kernel) when the activation rows do not fit one
+// CTA whole but their halves do; false when it does not apply.
+template <int FMT, int EPI>
+static bool launch_gemv_ks2(GemvParams p, cudaStream_t s) {
+    if constexpr (EPI == kEpiResidualPeer) {
+        return false;
+    } else {
+        constexpr int kMaxSmem = 224 * 1024;
+        constexpr int kStatic = kKs2MaxRb * 32 * 16 + kKs2MaxRb * 8 + 1024;  // peer slots, barriers, staging state
+        constexpr int UB = FMT == AMCU_WFMT_INT4 ? kW4PairBytes : 2048;
+        const int64_t G = p.k / 128;
+        if (G % 2 != 0 || p.norm_w != nullptr || p.m > kGemvMaxM) return false;
+        const int64_t kh = G / 2 * 128;
+        int su = 0, stages = 0;
+        for (int cap : {0, 16, 8}) {
+            su = stage_units<FMT>(kh, cap);
+            stages = 8;
+            while (stages > 2 && gemv_smem<FMT>((int)p.m, kh, su * UB, stages).total + kStatic > kMaxSmem) --stages;
+            if (gemv_smem<FMT>((int)p.m, kh, su * UB, stages).total + kStatic <= kMaxSmem) break;
+            stages = 0;
+        }
+        if (stages == 0) return false;
+        const int64_t nrb = p.n / 16, clusters = num_sms() / 2;
+        const int64_t per = (nrb + clusters - 1) / clusters;
+        if (per > kKs2MaxRb) return false;
+        p.stages = stages;
+        p.stage_units = su;
+        p.rb_per_cta = (int)per;
+        const int64_t grid = 2 * ((nrb + per - 1) / per);
+        const size_t smem = (size_t)gemv_smem<FMT>((int)p.m, kh, su * UB, stages).total;
+        set_func_attr_once((const void*)gemv_ks2_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+        launch_pdl(gemv_ks2_kernel<FMT, EPI>, dim3((unsigned)grid), dim3(kGemvThreads), smem, s, p);
+        return true;
+    }
+}
+
 template <int FMT, int EPI>
 static void launch_gemv_one(GemvParams p, cudaStream_t s) {
     constexpr int kMaxSmem = 224 * 1024;
@@ -267,6 +474,7 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
     // slices (each slice streams W again).
     int64_t fit = p.m;
     while (fit > 1 && gemv_smem<FMT>((int)fit, p.k, stage_units<FMT>(p.k, 16) * UB, 2).total > per_cta1) --fit;
+    if (fit < p.m && launch_gemv_ks2<FMT, EPI>(p, s)) return;  // halves of K instead of row slices
     {
         const int64_t slices = (p.m + fit - 1) / fit;
         fit = (p.m + slices - 1) / slices;

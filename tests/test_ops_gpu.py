@@ -472,6 +472,33 @@ def test_attention_prefill_shapes(ops, orc, nq, nkv, d, R, B):
         np.testing.assert_allclose(got[b * R:(b + 1) * R], ref, rtol=BF_RTOL, atol=BF_ATOL)
 
 
+@pytest.mark.parametrize("fmt", ["int4", "int8"])
+@pytest.mark.parametrize("m,k", [(8, 14336), (7, 16384), (8, 4096 * 3)])
+@pytest.mark.parametrize("residual", [False, True])
+def test_gemv_k_split_cluster(ops, orc, fmt, m, k, residual):
+    """Activation rows too long to stage whole in one CTA (8 x 14336 bf16)
+    take the 2-CTA cluster that splits K (each CTA stages half of every row,
+    rank 1 hands its partials to rank 0 through distributed shared memory):
+    against the oracle, including the residual epilogue applied by rank 0."""
+    from aethermind_b200 import _lib as L
+    n = 4096
+    pw, host = _w(ops, orc, fmt, n, k, seed=k + m)
+    rng = np.random.default_rng(k)
+    x = orc.bf16_round(rng.normal(0, 1, (m, k)).astype(np.float32))
+    ref = _oracle_linear(orc, fmt, x, host)
+    if residual:
+        res = orc.bf16_round(rng.normal(0, 1, (m, n)).astype(np.float32))
+        xr = bf16_dev(res)
+        y = ops.linear(bf16_dev(x), pw, epilogue=L.EPI_RESIDUAL_ADD, residual=xr, out=xr)
+        ref = orc.bf16_round(res + ref)
+    else:
+        y = ops.linear(bf16_dev(x), pw)
+    np.testing.assert_allclose(to_np(y), ref, rtol=BF_RTOL, atol=5e-2 if residual else BF_ATOL)
+    import ctypes as C
+    err = C.c_int32(0)
+    assert L.lib().amcu_device_error(C.byref(err), 1) == 0 and err.value == 0  # no wait ran out
+
+
 # ------------------------------------------------------------- elementwise
 @pytest.mark.parametrize("nq,nkv,d", [(32, 8, 128), (32, 8, 64), (16, 8, 128), (8, 8, 64)])
 def test_fused_rope_attention_matches_two_step_path(ops, orc, nq, nkv, d):

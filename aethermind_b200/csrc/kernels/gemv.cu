@@ -467,7 +467,16 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
     constexpr int kMaxSmem = 224 * 1024;
     const int smem_sm = smem_per_sm();
     constexpr int UB = FMT == AMCU_WFMT_INT4 ? kW4PairBytes : 2048;
-    const int per_cta2 = smem_sm / GEMV_CPS - 2048;  // GEMV_CPS CTAs per SM (room for the per-CTA reserve)
+    // CTAs per SM the rings are sized for: two (16 consumer warps per SM)
+    // for up to 5 activation rows; one with a deeper ring from 6 rows, whose
+    // staged rows would otherwise leave two shallow stages (8 rows: q/k/v
+    // 12.1 -> 10.2 us, o 10.3 -> 8.9, gate/up 20.9 -> 19.6; 1 row: 2 per SM
+    // is faster)
+    auto per_cta_for = [&](int rows) {
+        const int cps = rows >= 6 ? 1 : GEMV_CPS;
+        const int b = smem_sm / cps - 2048;  // room for the per-CTA reserve
+        return b < kMaxSmem ? b : kMaxSmem;
+    };
     const int per_cta1 = kMaxSmem;                  // one CTA per SM
     // The activation rows are staged in shared memory; when the m rows of this
     // K do not fit beside a ring of two 16-record stages, they go in equal
@@ -479,12 +488,13 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
         const int64_t slices = (p.m + fit - 1) / fit;
         fit = (p.m + slices - 1) / slices;
     }
-    // Ring geometry for a slice of `rows`: GEMV_CPS CTAs per SM with the
+    // Ring geometry for a slice of `rows`: per_cta_for(rows) bytes per CTA with the
     // largest stages (up to 32 records; 16 or 8 when the rows are long) that
     // leave two of them; else one CTA per SM with as many stages (2..8) as
     // fit. The grid is sized for the CTAs resident at once, so no CTA waits
     // for a second wave.
     auto plan = [&](int rows, int& su, int& stages, int& per_sm) {
+        const int per_cta2 = per_cta_for(rows);
         for (int cap : {0, 16, 8}) {
             su = stage_units<FMT>(p.k, cap);
             if (gemv_smem<FMT>(rows, p.k, su * UB, 2).total <= per_cta2) {

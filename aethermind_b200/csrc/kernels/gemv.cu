@@ -467,16 +467,7 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
     constexpr int kMaxSmem = 224 * 1024;
     const int smem_sm = smem_per_sm();
     constexpr int UB = FMT == AMCU_WFMT_INT4 ? kW4PairBytes : 2048;
-    // CTAs per SM the rings are sized for: two (16 consumer warps per SM)
-    // for up to 5 activation rows; one with a deeper ring from 6 rows, whose
-    // staged rows would otherwise leave two shallow stages (8 rows: q/k/v
-    // 12.1 -> 10.2 us, o 10.3 -> 8.9, gate/up 20.9 -> 19.6; 1 row: 2 per SM
-    // is faster)
-    auto per_cta_for = [&](int rows) {
-        const int cps = rows >= 6 ? 1 : GEMV_CPS;
-        const int b = smem_sm / cps - 2048;  // room for the per-CTA reserve
-        return b < kMaxSmem ? b : kMaxSmem;
-    };
+    const int per_cta2 = smem_sm / GEMV_CPS - 2048;  // GEMV_CPS CTAs per SM (room for the per-CTA reserve)
     const int per_cta1 = kMaxSmem;                  // one CTA per SM
     // The activation rows are staged in shared memory; when the m rows of this
     // K do not fit beside a ring of two 16-record stages, they go in equal
@@ -488,23 +479,23 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
         const int64_t slices = (p.m + fit - 1) / fit;
         fit = (p.m + slices - 1) / slices;
     }
-    // Ring geometry for a slice of `rows`: per_cta_for(rows) bytes per CTA with the
-    // largest stages (up to 32 records; 16 or 8 when the rows are long) that
-    // leave two of them; else one CTA per SM with as many stages (2..8) as
-    // fit. The grid is sized for the CTAs resident at once, so no CTA waits
-    // for a second wave.
+    // Ring geometry for a slice of `rows`: GEMV_CPS (2) CTAs per SM, 16
+    // consumer warps, while two full stages (32 INT4 records, the largest
+    // divisor of k/128 up to 32) fit beside the staged rows; otherwise one CTA
+    // per SM with a deeper ring (2..8 stages), because the two-CTA ring would
+    // be two shallow stages and leave too few bytes in flight (8 rows: q/k/v
+    // 12.1 -> 10.2 us, o 10.3 -> 8.9, gate/up 20.9 -> 19.6; the 70B down
+    // projection, 57 KB of staged row: 32.4 -> 29.8; every shape that keeps
+    // two full stages is faster with two CTAs). The grid is sized for the CTAs
+    // resident at once, so no CTA waits for a second wave.
     auto plan = [&](int rows, int& su, int& stages, int& per_sm) {
-        const int per_cta2 = per_cta_for(rows);
-        for (int cap : {0, 16, 8}) {
-            su = stage_units<FMT>(p.k, cap);
-            if (gemv_smem<FMT>(rows, p.k, su * UB, 2).total <= per_cta2) {
-                stages = 8;
-                while (stages > 2 && gemv_smem<FMT>(rows, p.k, su * UB, stages).total > per_cta2) --stages;
-                per_sm = smem_sm / (gemv_smem<FMT>(rows, p.k, su * UB, stages).total + 1024);
-                return;
-            }
-        }
         su = stage_units<FMT>(p.k);
+        if (gemv_smem<FMT>(rows, p.k, su * UB, 2).total <= per_cta2) {
+            stages = 8;
+            while (stages > 2 && gemv_smem<FMT>(rows, p.k, su * UB, stages).total > per_cta2) --stages;
+            per_sm = smem_sm / (gemv_smem<FMT>(rows, p.k, su * UB, stages).total + 1024);
+            return;
+        }
         if (gemv_smem<FMT>(rows, p.k, su * UB, 2).total > per_cta1) su = stage_units<FMT>(p.k, 16);
         stages = 8;
         while (stages > 2 && gemv_smem<FMT>(rows, p.k, su * UB, stages).total > per_cta1) --stages;

@@ -108,7 +108,10 @@ class ClockSampler:
 
 # (n, k) of the 8B decode GEMVs (q/k/v fused, o, gate/up interleaved, down, lm_head)
 GEMV_SHAPES_8B = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (2 * 14336, 4096), "down": (4096, 14336),
-                  "lm_head": (128256, 4096)}
+                  "lm_head": (128256, 4096),
+                  # the 70B-shaped model's (hidden 8192, 64 / 8 heads, intermediate 28672)
+                  "70b_qkv": (10240, 8192), "70b_o": (8192, 8192), "70b_gate_up": (2 * 28672, 8192),
+                  "70b_down": (8192, 28672)}
 
 
 def gemv_roofline(hbm_peak: float, ncopy: int | None = None, reps: int | None = None, m: int = 1,
@@ -354,7 +357,9 @@ def main() -> None:
     ap.add_argument("--decode", default="per-op", choices=["per-op", "persistent"],
                     help="decode plan: one kernel per op, or the persistent all-layers kernel (batch 1)")
     ap.add_argument("--nccl-allreduce", action="store_true", help="TP: NCCL for every all-reduce (no peer-memory one-shot)")
-    ap.add_argument("--op", default=None, help="time one kernel instead: gemv_{qkv,o,gate_up,down,lm_head} | gemm_gate_up")
+    ap.add_argument("--op", default=None,
+                    help="time one kernel instead: gemv_<shape> (qkv, o, gate_up, down, lm_head, 70b_qkv, 70b_o, "
+                         "70b_gate_up, 70b_down) | gemm_gate_up")
     ap.add_argument("--copies", type=int, default=None, help="--op gemv_*: weight copies rotated")
     ap.add_argument("--m", type=int, default=1, help="--op gemv_*: activation rows")
     ap.add_argument("--reps", type=int, default=None, help="--op: timed launches")

@@ -274,6 +274,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreads, 1) gem
     cluster.sync();  // rank 0's barriers exist before rank 1 can arrive on them
 
     if (warp == kGemvConsumers) {
+        // this warp stays resident until the final cluster barrier: it lets
+        // the next kernel launch like the consumers do
+        pdl_trigger();
         if (lane == 0) {
             int slot = 0;
             uint32_t phase = 0;

@@ -606,15 +606,19 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
                 return pb.Add(OpType::kLinear, lin, {in, View2(s->x.data(), A, M, H, H)}, {MView2(s->x.data(), A, M, H, H)},
                               &res, &W.w, p + name);
             }
-            // decode GEMV: the ranks' partials are summed over peer memory in
-            // the GEMV's own epilogue, residual added there (one launch)
-            // On by default (AMCU_TP_FUSED_ALLREDUCE=0 selects the separate
-            // one-shot kernel): on 2 B200s the 8B decode step measured 1.937
-            // ms/token fused, 1.941 with the one-shot kernel, 2.035 with NCCL.
-            static const bool fused_ok = [] {
+            // decode GEMV on 2 ranks: the partials are summed over peer memory
+            // in the GEMV's own epilogue, residual added there (one launch).
+            // On 2 B200s the 8B decode step measured 1.937 ms/token fused,
+            // 1.941 with the one-shot kernel, 2.035 with NCCL. From 3 ranks the
+            // separate one-shot kernel: each row block's wait for every peer
+            // holds its CTA in step with the slowest rank, which on 4 B200s
+            // cost 2.59 ms/token against 1.71 with the one-shot kernel (2.07
+            // with NCCL). AMCU_TP_FUSED_ALLREDUCE=0 / =1 forces either way.
+            static const int fused_env = [] {
                 const char* v = std::getenv("AMCU_TP_FUSED_ALLREDUCE");
-                return !(v && v[0] == '0');
+                return v ? (v[0] == '0' ? 0 : 1) : -1;
             }();
+            const bool fused_ok = fused_env == 1 || (fused_env < 0 && m->rt->tp_size <= 2);
             if (fused_ok && phase == ExecPhase::kDecode && M <= 8 && wf != WeightFormat::kPlain && A == DType::kBF16 &&
                 m->rt->comm.PeerReduceArgs() != nullptr && H * 8 <= 16384 * 8) {
                 LinearAttrs res{AMCU_EPI_RESIDUAL_ADD};

@@ -53,7 +53,9 @@ def bench_config(world: int, nccl_allreduce: bool, layers: int) -> dict:
     """The workload description both arms print (same keys, same values)."""
     return {"workload": WORKLOAD, "global_batch": 1, "seq_len": PROMPT + NEW, "parallelism": f"tp{world}",
             "allreduce": "none" if world == 1 else ("nccl" if nccl_allreduce else
-                                                    "peer memory inside the o/down GEMV epilogue (decode), nccl (prefill)"),
+                                                    ("peer memory inside the o/down GEMV epilogue" if world == 2 else
+                                                     "one-shot peer-memory kernel after the o/down GEMV")
+                                                    + " (decode), nccl (prefill)"),
             "l2": "weights (3.9 GB) exceed L2; no flush needed", "layers": layers}
 
 

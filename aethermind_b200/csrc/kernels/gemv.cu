@@ -27,6 +27,8 @@
 #include <cooperative_groups.h>
 
 #include "../amcu_internal.h"
+#include <cstdlib>
+
 #include "allreduce.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
@@ -71,8 +73,8 @@ namespace amcu {
 // last-arriver combine) measured slower, 17.4 against 13.3 us for the 8B
 // gate/up: the free slots let the next kernel's CTAs start early under PDL and
 // fetch their weights while this one finishes, which outweighs the balance.
-template <int FMT, int EPI, bool M1>
-__global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvParams p) {
+template <int FMT, int EPI, bool M1, int NC>
+__global__ void __launch_bounds__((NC + 1) * 32, NC == kGemvConsumers ? GEMV_MINB : 1) gemv_tc_kernel(GemvParams p) {
     constexpr bool W4 = FMT == AMCU_WFMT_INT4;
     constexpr int UB = W4 ? kW4PairBytes : 2048;  // bytes per 128-column group unit
     extern __shared__ __align__(128) uint8_t smem[];
@@ -83,7 +85,7 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
     const int G = (int)(p.k / 128);              // group units per row block
     const int M = (int)p.m;
     const int xrow = (int)(p.k * 2 + kXPad);
-    const GemvSmem L = gemv_smem<FMT>(M, p.k, SBY, S);
+    const GemvSmem L = gemv_smem<FMT, NC>(M, p.k, SBY, S);
     float4* red = reinterpret_cast<float4*>(smem + L.red);  // [2][consumers][32]
     float* sx = reinterpret_cast<float*>(smem + L.sx);      // [G][8] (INT4)
     uint8_t* xs = smem + L.xs;                              // [M][k] bf16 (+pad)
@@ -101,14 +103,14 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kGemvConsumers);
+            mbar_init(&empty[s], NC);
         }
         fence_mbar_init();
         l2_prefetch_share(p.l2_next);
     }
     __syncthreads();
 
-    if (warp == kGemvConsumers) {
+    if (warp == NC) {
         // ---- producer: weights do not depend on earlier kernels, so the ring
         // fills while the previous kernel finishes.
         if (lane == 0) {
@@ -139,11 +141,11 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
     {
         StageCtx sc{static_cast<const __nv_bfloat16*>(p.x), p.x_stride, p.k, M,
                     static_cast<const __nv_bfloat16*>(p.norm_w), p.eps, xs, xrow, sx, &stsh,
-                    (int)threadIdx.x, kGemvConsumers * 32, 2};
+                    (int)threadIdx.x, NC * 32, 2};
         stage_activations<W4>(sc);
     }
     const float* row_mul = stsh.row_mul;
-    constexpr int NT = kGemvConsumers * 32;
+    constexpr int NT = NC * 32;
     const float rm0 = 2 * t < M ? row_mul[2 * t] : 1.f, rm1 = 2 * t + 1 < M ? row_mul[2 * t + 1] : 1.f;
 
     // Lanes whose activation row does not exist (g >= M) read row 0: they only
@@ -162,7 +164,7 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
             fail_i = i;
             if (lane == 0) record_device_error(p.err, kErrGemvFullWait);
         }
-        gemv_stage<FMT, M1>(ring + slot * SBY, len, xrow_g, sx, grp0, warp, lane, g, t, acc);
+        gemv_stage<FMT, M1, NC>(ring + slot * SBY, len, xrow_g, sx, grp0, warp, lane, g, t, acc);
         __syncwarp();  // every lane has read the stage
         if (lane == 0) mbar_arrive(&empty[slot]);
         if (++slot == S) {
@@ -173,13 +175,13 @@ __global__ void __launch_bounds__(kGemvThreads, GEMV_MINB) gemv_tc_kernel(GemvPa
     // row-block end: publish this warp's partial tile, meet the other warps,
     // and let one warp reduce and apply the epilogue
     auto finish = [&](int rb) {
-        red[(par * kGemvConsumers + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        red[(par * NC + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         named_bar_sync(1, NT);
-        if (warp == rb % kGemvConsumers) {
+        if (warp == rb % NC) {
             float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int w = 0; w < kGemvConsumers; ++w) {
-                const float4 v = red[(par * kGemvConsumers + w) * 32 + lane];
+            for (int w = 0; w < NC; ++w) {
+                const float4 v = red[(par * NC + w) * 32 + lane];
                 s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
             }
             gemv_epilogue<FMT, EPI>(p, rb, g, t, s4, rm0, rm1);
@@ -232,7 +234,7 @@ __device__ __forceinline__ bool mbar_wait_acq_cluster(uint64_t* bar, uint32_t pa
 }
 
 template <int FMT, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreads, 1) gemv_ks2_kernel(GemvParams p) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreadsWide, 1) gemv_ks2_kernel(GemvParams p) {
     constexpr bool W4 = FMT == AMCU_WFMT_INT4;
     constexpr int UB = W4 ? kW4PairBytes : 2048;
     cg::cluster_group cluster = cg::this_cluster();
@@ -246,7 +248,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreads, 1) gem
     const int64_t kh = (int64_t)GH * 128;
     const int M = (int)p.m;
     const int xrow = (int)(kh * 2 + kXPad);
-    const GemvSmem L = gemv_smem<FMT>(M, kh, SBY, S);
+    const GemvSmem L = gemv_smem<FMT, kGemvConsumersWide>(M, kh, SBY, S);
     float4* red = reinterpret_cast<float4*>(smem + L.red);
     float* sx = reinterpret_cast<float*>(smem + L.sx);
     uint8_t* xs = smem + L.xs;
@@ -265,7 +267,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreads, 1) gem
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kGemvConsumers);
+            mbar_init(&empty[s], kGemvConsumersWide);
         }
         for (int r = 0; r < kKs2MaxRb; ++r) mbar_init(&peer_bar[r], 1);
         fence_mbar_init();
@@ -273,7 +275,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreads, 1) gem
     }
     cluster.sync();  // rank 0's barriers exist before rank 1 can arrive on them
 
-    if (warp == kGemvConsumers) {
+    if (warp == kGemvConsumersWide) {
         // this warp stays resident until the final cluster barrier: it lets
         // the next kernel launch like the consumers do
         pdl_trigger();
@@ -302,7 +304,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreads, 1) gem
         __shared__ StageShared stsh;
         {
             StageCtx sc{static_cast<const __nv_bfloat16*>(p.x) + (int64_t)rank * kh, p.x_stride, kh, M, nullptr,
-                        p.eps, xs, xrow, sx, &stsh, (int)threadIdx.x, kGemvConsumers * 32, 2};
+                        p.eps, xs, xrow, sx, &stsh, (int)threadIdx.x, kGemvConsumersWide * 32, 2};
             stage_activations<W4>(sc);
         }
         const float rm0 = 2 * t < M ? stsh.row_mul[2 * t] : 1.f, rm1 = 2 * t + 1 < M ? stsh.row_mul[2 * t + 1] : 1.f;
@@ -324,7 +326,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreads, 1) gem
                     fail_i = i;
                     if (lane == 0) record_device_error(p.err, kErrGemvFullWait);
                 }
-                gemv_stage<FMT, false>(ring + slot * SBY, SU, xrow_g, sx, j * SU, warp, lane, g, t, acc);
+                gemv_stage<FMT, false, kGemvConsumersWide>(ring + slot * SBY, SU, xrow_g, sx, j * SU, warp, lane, g, t, acc);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[slot]);
                 if (++slot == S) {
@@ -332,13 +334,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreads, 1) gem
                     phase ^= 1;
                 }
             }
-            red[(par * kGemvConsumers + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            named_bar_sync(1, kGemvConsumers * 32);
-            if (warp == r % kGemvConsumers) {
+            red[(par * kGemvConsumersWide + warp) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            named_bar_sync(1, kGemvConsumersWide * 32);
+            if (warp == r % kGemvConsumersWide) {
                 float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                for (int w = 0; w < kGemvConsumers; ++w) {
-                    const float4 v = red[(par * kGemvConsumers + w) * 32 + lane];
+                for (int w = 0; w < kGemvConsumersWide; ++w) {
+                    const float4 v = red[(par * kGemvConsumersWide + w) * 32 + lane];
                     s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
                 }
                 // this half's rows at their true scale (the guards may differ per half)
@@ -418,14 +420,19 @@ __global__ void gemm_plain_kernel(GemvParams p) {
 }
 
 template <int FMT, int EPI>
-static void launch_gemv_variant(const GemvParams& q, int64_t grid, size_t smem, cudaStream_t s) {
+static void launch_gemv_variant(const GemvParams& q, int64_t grid, size_t smem, bool wide, cudaStream_t s) {
     constexpr int kMaxSmem = 224 * 1024;
-    auto go = [&](auto kern) {
+    auto go = [&](auto kern, int nc) {
         set_func_attr_once((const void*)kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-        launch_pdl(kern, dim3((unsigned)grid), dim3(kGemvThreads), smem, s, q);
+        launch_pdl(kern, dim3((unsigned)grid), dim3((nc + 1) * 32), smem, s, q);
     };
-    if (q.m == 1) go(gemv_tc_kernel<FMT, EPI, true>);
-    else go(gemv_tc_kernel<FMT, EPI, false>);
+    if (wide) {
+        if (q.m == 1) go(gemv_tc_kernel<FMT, EPI, true, kGemvConsumersWide>, kGemvConsumersWide);
+        else go(gemv_tc_kernel<FMT, EPI, false, kGemvConsumersWide>, kGemvConsumersWide);
+    } else {
+        if (q.m == 1) go(gemv_tc_kernel<FMT, EPI, true, kGemvConsumers>, kGemvConsumers);
+        else go(gemv_tc_kernel<FMT, EPI, false, kGemvConsumers>, kGemvConsumers);
+    }
 }
 
 // The 2-CTA K split (gemv_ks2_kernel) when the activation rows do not fit one
@@ -445,8 +452,8 @@ static bool launch_gemv_ks2(GemvParams p, cudaStream_t s) {
         for (int cap : {0, 16, 8}) {
             su = stage_units<FMT>(kh, cap);
             stages = 8;
-            while (stages > 2 && gemv_smem<FMT>((int)p.m, kh, su * UB, stages).total + kStatic > kMaxSmem) --stages;
-            if (gemv_smem<FMT>((int)p.m, kh, su * UB, stages).total + kStatic <= kMaxSmem) break;
+            while (stages > 2 && gemv_smem<FMT, kGemvConsumersWide>((int)p.m, kh, su * UB, stages).total + kStatic > kMaxSmem) --stages;
+            if (gemv_smem<FMT, kGemvConsumersWide>((int)p.m, kh, su * UB, stages).total + kStatic <= kMaxSmem) break;
             stages = 0;
         }
         if (stages == 0) return false;
@@ -457,10 +464,11 @@ static bool launch_gemv_ks2(GemvParams p, cudaStream_t s) {
         p.stage_units = su;
         p.rb_per_cta = (int)per;
         const int64_t grid = 2 * ((nrb + per - 1) / per);
-        const size_t smem = (size_t)gemv_smem<FMT>((int)p.m, kh, su * UB, stages).total;
+        const size_t smem = (size_t)gemv_smem<FMT, kGemvConsumersWide>((int)p.m, kh, su * UB, stages).total;
+        // the largest dynamic size any call can ask for (set once per device)
         set_func_attr_once((const void*)gemv_ks2_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem);
-        launch_pdl(gemv_ks2_kernel<FMT, EPI>, dim3((unsigned)grid), dim3(kGemvThreads), smem, s, p);
+                           kMaxSmem - kStatic);
+        launch_pdl(gemv_ks2_kernel<FMT, EPI>, dim3((unsigned)grid), dim3(kGemvThreadsWide), smem, s, p);
         return true;
     }
 }
@@ -491,25 +499,32 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
     // projection, 57 KB of staged row: 32.4 -> 29.8; every shape that keeps
     // two full stages is faster with two CTAs). The grid is sized for the CTAs
     // resident at once, so no CTA waits for a second wave.
-    auto plan = [&](int rows, int& su, int& stages, int& per_sm) {
+    auto plan = [&](int rows, int& su, int& stages, int& per_sm, bool& wide) {
         su = stage_units<FMT>(p.k);
-        if (gemv_smem<FMT>(rows, p.k, su * UB, 2).total <= per_cta2) {
+        wide = false;
+        static const bool force_wide = [] {
+            const char* v = std::getenv("AMCU_GEMV_WIDE");
+            return v && v[0] == '1';
+        }();
+        if (!force_wide && gemv_smem<FMT>(rows, p.k, su * UB, 2).total <= per_cta2) {
             stages = 8;
             while (stages > 2 && gemv_smem<FMT>(rows, p.k, su * UB, stages).total > per_cta2) --stages;
             per_sm = smem_sm / (gemv_smem<FMT>(rows, p.k, su * UB, stages).total + 1024);
             return;
         }
-        if (gemv_smem<FMT>(rows, p.k, su * UB, 2).total > per_cta1) su = stage_units<FMT>(p.k, 16);
+        if (gemv_smem<FMT, kGemvConsumersWide>(rows, p.k, su * UB, 2).total > per_cta1) su = stage_units<FMT>(p.k, 16);
         stages = 8;
-        while (stages > 2 && gemv_smem<FMT>(rows, p.k, su * UB, stages).total > per_cta1) --stages;
+        while (stages > 2 && gemv_smem<FMT, kGemvConsumersWide>(rows, p.k, su * UB, stages).total > per_cta1) --stages;
         per_sm = 1;
+        wide = true;
     };
     const int64_t nrb = p.n / 16;
     for (int64_t m0 = 0; m0 < p.m; m0 += fit) {
         GemvParams q = p;
         q.m = p.m - m0 < fit ? p.m - m0 : fit;
         int su = 0, stages = 0, per_sm = 1;
-        plan((int)q.m, su, stages, per_sm);
+        bool wide = false;
+        plan((int)q.m, su, stages, per_sm, wide);
 #ifdef GEMV_GRID_CPS
         if (per_sm > GEMV_GRID_CPS) per_sm = GEMV_GRID_CPS;
 #endif
@@ -521,8 +536,11 @@ static void launch_gemv_one(GemvParams p, cudaStream_t s) {
         q.x = static_cast<const __nv_bfloat16*>(p.x) + m0 * p.x_stride;
         q.y = static_cast<__nv_bfloat16*>(p.y) + m0 * p.y_stride;
         if (p.residual) q.residual = static_cast<const __nv_bfloat16*>(p.residual) + m0 * p.y_stride;
-        const size_t smem = (size_t)gemv_smem<FMT>((int)q.m, p.k, su * UB, stages).total;
-        launch_gemv_variant<FMT, EPI>(q, grid, smem, s);
+        // one CTA per SM: 16 consumer warps share its staged rows (the
+        // unpack + MMA rate of 8 warps is about half of an SM's HBM share)
+        const size_t smem = (size_t)(wide ? gemv_smem<FMT, kGemvConsumersWide>((int)q.m, p.k, su * UB, stages).total
+                                          : gemv_smem<FMT>((int)q.m, p.k, su * UB, stages).total);
+        launch_gemv_variant<FMT, EPI>(q, grid, smem, wide, s);
     }
 }
 

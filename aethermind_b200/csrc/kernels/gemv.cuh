@@ -9,6 +9,8 @@ namespace amcu {
 
 constexpr int kGemvConsumers = 8;                     // consumer warps per GEMV CTA
 constexpr int kGemvThreads = (kGemvConsumers + 1) * 32;  // + one producer warp
+constexpr int kGemvConsumersWide = 16;               // consumer warps of a one-CTA-per-SM GEMV
+constexpr int kGemvThreadsWide = (kGemvConsumersWide + 1) * 32;
 constexpr int kGemvMaxM = 8;
 constexpr int kW4PairBytes = 2 * 512 + 32;  // INT4 pair record: two tiles + 16 fp16 scales
 

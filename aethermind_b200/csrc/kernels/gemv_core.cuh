@@ -171,12 +171,12 @@ constexpr int kXPad = 16;  // bytes of padding per staged activation row
 struct GemvSmem {
     int red, sx, xs, ring, bars, total;
 };
-template <int FMT>
+template <int FMT, int NC = kGemvConsumers>
 __host__ __device__ inline GemvSmem gemv_smem(int m, int64_t k, int stage_bytes, int stages) {
     auto up = [](int64_t v) { return (int)((v + 127) / 128 * 128); };
     GemvSmem s;
     s.red = 0;
-    s.sx = up(2 * kGemvConsumers * 32 * 16);
+    s.sx = up(2 * NC * 32 * 16);
     s.xs = s.sx + up(FMT == AMCU_WFMT_INT4 ? (k / 128) * 8 * 4 : 0);
     s.ring = s.xs + up(m * (k * 2 + kXPad));
     s.bars = s.ring + stages * stage_bytes;
@@ -248,27 +248,27 @@ __device__ __forceinline__ void gemv_unit(const uint8_t* rec, const uint8_t* xro
 }
 
 // The `len` units of a stage (groups grp0.. of one row block): warp w takes
-// units w, w + 8, ... Stages of 16 or 32 units get a fixed trip count, which
+// units w, w + NC, ... Stages of 16 or 32 units get a fixed trip count, which
 // lets the compiler overlap one unit's loads and unpack with the previous
 // unit's MMA chain.
-template <int FMT, bool M1>
+template <int FMT, bool M1, int NC = kGemvConsumers>
 __device__ __forceinline__ void gemv_stage(const uint8_t* st, int len, const uint8_t* xrow_g, const float* sx,
                                            int grp0, int warp, int lane, int g, int t, float (&acc)[4]) {
     constexpr int UB = FMT == AMCU_WFMT_INT4 ? kW4PairBytes : 2048;
-    if (len == 4 * kGemvConsumers) {
+    if (len == 4 * NC) {
 #pragma unroll
         for (int uu = 0; uu < 4; ++uu) {
-            const int u = warp + uu * kGemvConsumers;
+            const int u = warp + uu * NC;
             gemv_unit<FMT, M1>(st + u * UB, xrow_g, sx, grp0 + u, lane, g, t, acc);
         }
-    } else if (len == 2 * kGemvConsumers) {
+    } else if (len == 2 * NC) {
 #pragma unroll
         for (int uu = 0; uu < 2; ++uu) {
-            const int u = warp + uu * kGemvConsumers;
+            const int u = warp + uu * NC;
             gemv_unit<FMT, M1>(st + u * UB, xrow_g, sx, grp0 + u, lane, g, t, acc);
         }
     } else {
-        for (int u = warp; u < len; u += kGemvConsumers)
+        for (int u = warp; u < len; u += NC)
             gemv_unit<FMT, M1>(st + u * UB, xrow_g, sx, grp0 + u, lane, g, t, acc);
     }
 }

@@ -492,10 +492,10 @@ Status BuildPlan(am_session_s* s, ExecPhase phase, int64_t B, int64_t R, Executi
     // Decode GEMVs (m <= 8) stage their activations anyway: the RMSNorm in
     // front of q/k/v and gate/up runs there instead of as its own kernel.
     const bool fuse_norm = phase == ExecPhase::kDecode && wf != WeightFormat::kPlain && M <= 8;
-    // decode attention blocks as one fused RoPE + attention launch where a
-    // kernel for it is registered (bf16) and the session does not ask for
-    // the unfused steps
-    const bool fuse_attn = phase == ExecPhase::kDecode && R == B && s->cfg.unfused_attention == 0 &&
+    // decode attention blocks (one row per sequence, any batch) as one fused
+    // RoPE + attention launch where a kernel for it is registered (bf16) and
+    // the session does not ask for the unfused steps
+    const bool fuse_attn = phase == ExecPhase::kDecode && R == 1 && s->cfg.unfused_attention == 0 &&
                            m->rt->backend->ResolveKernelInfo(OpType::kRoPEAttention, act).ok();
     // Embedding
     {

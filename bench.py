@@ -145,7 +145,7 @@ def gemv_roofline(hbm_peak: float, ncopy: int | None = None, reps: int | None = 
     lib = L.lib()
     stream = torch.cuda.current_stream().cuda_stream
     for a in args[:4]:
-        lib.amcu_gemv_w4g128(C.byref(a), stream)
+        L.check(lib.amcu_gemv_w4g128(C.byref(a), stream), "amcu_gemv_w4g128")  # a failed launch is not timed
     torch.cuda.synchronize()
     reps = reps or 20 * ncopy
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -141,6 +141,8 @@ def test_plan_resolves_phase_kernels(sess_mod, rt):
     pre = s.plan_steps(0, 1, 16)
     assert any("GemvW4G128_CUDA_Decode" in l for l in dec)
     assert any("RoPEAttnDecodeCluster_CUDA_BF16" in l for l in dec)
+    # every batch size decodes one row per sequence: the fused kernel applies
+    assert any("RoPEAttnDecodeCluster_CUDA_BF16" in l for l in s.plan_steps(1, 2, 1))
     unf = sess_mod.Session(m, fused_attention=False).plan_steps(1, 1, 1)
     assert any("AttnDecodeSplitK" in l for l in unf)
     assert any("GemmW4G128_CUDA_Prefill" in l for l in pre)

@@ -25,6 +25,7 @@
 #include "../amcu_internal.h"
 #include "attn_decode.cuh"
 #include "common.cuh"
+#include "diag_timeline.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -51,6 +52,8 @@ struct RopeAttnParams {
 template <int GRP, int D, int CS>
 __global__ void __launch_bounds__(kRaThreads) attn_rope_decode_kernel(RopeAttnParams p) {
     cg::cluster_group cluster = cg::this_cluster();
+    DiagTl tl;
+    tl.entry();
     const int rank = (int)cluster.block_rank();
     const int kvh = blockIdx.y;
     const int64_t row = blockIdx.z;  // one row per sequence
@@ -77,6 +80,7 @@ __global__ void __launch_bounds__(kRaThreads) attn_rope_decode_kernel(RopeAttnPa
 
     pdl_wait();
     pdl_trigger();
+    tl.waited();
 
     __shared__ __align__(16) float qs[GRP][D];
     __shared__ float sm_m[kRaWarps][GRP], sm_l[kRaWarps][GRP];
@@ -93,6 +97,7 @@ __global__ void __launch_bounds__(kRaThreads) attn_rope_decode_kernel(RopeAttnPa
 
     DecodeWarpState<GRP, D> st;
     loop.run(qs, st);
+    if (threadIdx.x == 0) tl.mark();
     decode_publish_warp<GRP, D>(st, warp, lane, sm_m, sm_l, sm_o);
     __syncthreads();
     for (int e = threadIdx.x; e < GRP * D; e += kRaThreads) {
@@ -133,6 +138,7 @@ __global__ void __launch_bounds__(kRaThreads) attn_rope_decode_kernel(RopeAttnPa
         p.out[row * p.out_stride + (int64_t)kvh * GRP * D + e] = __float2bfloat16_rn(O / Ls);
     }
     cluster.sync();  // partials stay alive until every CTA has read them
+    if (threadIdx.x == 0) tl.done(2000u + CS);
 }
 
 template <int GRP, int D, int CS>
@@ -271,3 +277,8 @@ extern "C" am_status_code amcu_attn_decode_rope(const AmcuRopeKvArgs* r, const A
     if (!ok) return set_error(AM_STATUS_INVALID_ARGUMENT, "amcu_attn_decode_rope: GQA group %d unsupported", grp);
     return check_launch("amcu_attn_decode_rope");
 }
+
+#ifdef AMCU_DIAG
+// Diagnostics: the fused decode attention launch timeline (see diag_timeline.cuh).
+extern "C" __attribute__((visibility("default"))) int amcu_diag_timeline_attn(void* out, int max) { return amcu::diag_timeline_take(out, max); }
+#endif

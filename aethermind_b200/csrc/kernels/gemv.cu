@@ -30,6 +30,7 @@
 #include <cstdlib>
 
 #include "allreduce.cuh"
+#include "diag_timeline.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 #include "gemv_core.cuh"
@@ -75,6 +76,8 @@ namespace amcu {
 // fetch their weights while this one finishes, which outweighs the balance.
 template <int FMT, int EPI, bool M1, int NC>
 __global__ void __launch_bounds__((NC + 1) * 32, NC == kGemvConsumers ? GEMV_MINB : 1) gemv_tc_kernel(GemvParams p) {
+    DiagTl tl;
+    tl.entry();
     constexpr bool W4 = FMT == AMCU_WFMT_INT4;
     constexpr int UB = W4 ? kW4PairBytes : 2048;  // bytes per 128-column group unit
     extern __shared__ __align__(128) uint8_t smem[];
@@ -135,6 +138,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, NC == kGemvConsumers ? GEMV_MIN
 
     pdl_wait();
     pdl_trigger();
+    tl.waited();
 
     // ---- stage the activations (fused RMSNorm; INT4: fp16 + group sums)
     __shared__ StageShared stsh;
@@ -202,6 +206,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, NC == kGemvConsumers ? GEMV_MIN
                 break;
             }
     }
+    AMCU_DIAG_TL(named_bar_sync(1, NT); if (threadIdx.x == 0) tl.done(1000u + 10u * EPI + (NC == kGemvConsumers ? 0u : 1u));)
 }
 
 // K split over a 2-CTA thread-block cluster, for activation rows too long to
@@ -838,3 +843,8 @@ am_status_code amcu_unpack_weight(int32_t format, int32_t dtype, int64_t n, int6
 }
 
 }  // extern "C"
+
+#ifdef AMCU_DIAG
+// Diagnostics: the GEMV launch timeline (see diag_timeline.cuh).
+extern "C" __attribute__((visibility("default"))) int amcu_diag_timeline_gemv(void* out, int max) { return amcu::diag_timeline_take(out, max); }
+#endif

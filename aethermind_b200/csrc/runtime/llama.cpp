@@ -439,11 +439,16 @@ MutableTensorView MView2(void* p, DType dt, int64_t rows, int64_t cols, int64_t 
     return v;
 }
 
-// Weight prefetch across kernel boundaries: every quantized Linear step asks
-// for the next Linear step's weights and scales to be pulled into L2 while it
-// runs (the last step of the plan asks for the first one's, which the next
-// decode step reads), and for the one after that too when the next weight is
-// small, so HBM keeps streaming through the short kernels in between.
+// Weight prefetch across kernel boundaries (off unless AMCU_L2_HINTS asks):
+// a quantized Linear step can ask for the next Linear step's weights and
+// scales to be pulled into L2 while it runs (the last step of the plan asks
+// for the first one's, which the next decode step reads), and for the one
+// after that too when the next weight is small. Measured on the 8B batch-1
+// decode step, the hints cost more than they save: the prefetch traffic
+// (67 MB asked for by each q/k/v projection) competes with the latency-bound
+// loads of the kernels in between. Per-launch timeline, us per layer:
+// q/k/v 9.5 -> 7.6, o 6.4 -> 5.5, down 13.7 -> 12.8 without hints; decode
+// 581 -> 624 tok/s, batch 8 3004 -> 3249, 70B 90.2 -> 96.8, 1B 1530 -> 1505.
 void SetL2Hints(ExecutionPlan& plan) {
     constexpr uint64_t kMaxRange = 64ull << 20;   // L2 is 126 MB
     constexpr uint64_t kSmallWeight = 16ull << 20;
@@ -452,7 +457,13 @@ void SetL2Hints(ExecutionPlan& plan) {
         const auto* w = static_cast<const AmcuWeight*>(plan.steps[i].packed_weights);
         if (plan.steps[i].op == OpType::kLinear && w && w->format != AMCU_WFMT_PLAIN) lin.push_back(i);
     }
-    if (lin.size() < 2) return;
+    // AMCU_L2_HINTS: 0 (default) = no hints, 1 = the next weight only,
+    // 2 = the next weight and, after a small one, the one after it
+    static const int mode = [] {
+        const char* v = std::getenv("AMCU_L2_HINTS");
+        return v ? std::atoi(v) : 0;
+    }();
+    if (lin.size() < 2 || mode == 0) return;
     auto weight_of = [&](size_t j) { return static_cast<const AmcuWeight*>(plan.steps[lin[j % lin.size()]].packed_weights); };
     auto wbytes = [](const AmcuWeight* w) {
         return (uint64_t)amcu_packed_weight_bytes(w->format, w->dtype, w->n, w->k, w->group);
@@ -467,7 +478,7 @@ void SetL2Hints(ExecutionPlan& plan) {
             h.bytes[slot++] = b < kMaxRange ? b : kMaxRange;
             h.ptr[slot] = w->scales;
             h.bytes[slot++] = (uint64_t)amcu_packed_scale_bytes(w->format, w->n, w->k, w->group);
-            if (b >= kSmallWeight) break;
+            if (b >= kSmallWeight || mode == 1) break;
         }
         reinterpret_cast<AmcuLinearArgs*>(plan.steps[lin[j]].params.data())->l2_next = h;
     }

@@ -31,7 +31,14 @@ namespace cg = cooperative_groups;
 
 namespace amcu {
 
-constexpr int kRaWarps = 4;  // warps per CTA of the fused kernel
+// Warps per CTA of the fused kernel. 8 warps halve a CTA's key loop at
+// context ~520 (2.3 against 3.6 us), but 16-CTA clusters of 256 threads
+// become resident only as the q/k/v GEMV drains: the launch spans 14.6 us
+// against 9.3 and the 8B decode runs 588 against 623 tok/s.
+#ifndef AMCU_RA_WARPS
+#define AMCU_RA_WARPS 4
+#endif
+constexpr int kRaWarps = AMCU_RA_WARPS;
 constexpr int kRaThreads = kRaWarps * 32;
 constexpr int kRaTargetCtas = 256;  // CTAs of one launch the cluster size aims at (batch 8, 8 kv heads: 4 per cluster)
 
@@ -94,6 +101,7 @@ __global__ void __launch_bounds__(kRaThreads) attn_rope_decode_kernel(RopeAttnPa
         rope_append_kv<D>(p.k + row * p.k_stride + (int64_t)kvh * D, p.v + row * p.v_stride + (int64_t)kvh * D,
                           kbase + pos * D, vbase + pos * D, pos, p.cos_sin, p.theta, threadIdx.x, kRaThreads);
     __syncthreads();  // q staged; the appended row is visible to this CTA's reads
+    if (threadIdx.x == 0) tl.mark2();
 
     DecodeWarpState<GRP, D> st;
     loop.run(qs, st);
@@ -113,11 +121,21 @@ __global__ void __launch_bounds__(kRaThreads) attn_rope_decode_kernel(RopeAttnPa
     cluster.sync();  // every CTA's partial is complete
 
     // This CTA combines outputs [rank * per, (rank + 1) * per); all CS
-    // partials of an element are fetched with independent loads.
+    // partials of an element are fetched with independent loads. Once every
+    // read of the other CTAs' shared memory is done the CTA arrives on the
+    // cluster barrier, stores its outputs, and only then waits: the partials
+    // stay alive until every CTA has read them, and the store overlaps the
+    // barrier.
     constexpr int per = GRP * D / CS;
-    for (int j = threadIdx.x; j < per; j += kRaThreads) {
+    constexpr int kIter = (per + kRaThreads - 1) / kRaThreads;
+    float res[kIter];
+#pragma unroll
+    for (int it = 0; it < kIter; ++it) {
+        const int j = threadIdx.x + it * kRaThreads;
+        res[it] = 0.f;
+        if (j >= per) continue;
         const int e = rank * per + j;
-        const int h = e / D, dd = e % D;
+        const int h = e / D;
         float mr[CS], lr[CS], orr[CS];
 #pragma unroll
         for (int r = 0; r < CS; ++r) {
@@ -135,9 +153,15 @@ __global__ void __launch_bounds__(kRaThreads) attn_rope_decode_kernel(RopeAttnPa
             Ls += lr[r] * f;
             O += orr[r] * f;
         }
-        p.out[row * p.out_stride + (int64_t)kvh * GRP * D + e] = __float2bfloat16_rn(O / Ls);
+        res[it] = O / Ls;
     }
-    cluster.sync();  // partials stay alive until every CTA has read them
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+#pragma unroll
+    for (int it = 0; it < kIter; ++it) {
+        const int j = threadIdx.x + it * kRaThreads;
+        if (j < per) p.out[row * p.out_stride + (int64_t)kvh * GRP * D + rank * per + j] = __float2bfloat16_rn(res[it]);
+    }
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
     if (threadIdx.x == 0) tl.done(2000u + CS);
 }
 

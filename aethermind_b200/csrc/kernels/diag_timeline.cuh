@@ -1,7 +1,7 @@
 // Diagnostics (AMCU_DIAG builds only; the default build compiles all of this
 // out): a per-CTA launch timeline. Every instrumented CTA appends one record
 // with its SM, the globaltimer at entry, when its dependency wait returned,
-// one optional mark in between (field pad) and when its work was done. Each
+// up to two marks in between (fields pad, pad2) and when its work was done. Each
 // translation unit that includes this header keeps its own log (file-scope
 // device arrays); its amcu_diag_timeline_*
 // export copies the log out and resets it. The host merges the logs by time:
@@ -14,7 +14,7 @@ namespace amcu {
 
 struct DiagTlRec {
     uint32_t tag, cta, smid, grid;
-    unsigned long long t_entry, t_wait, t_done, pad;
+    unsigned long long t_entry, t_wait, t_done, pad, pad2, pad3, pad4, pad5;
 };
 
 #ifdef AMCU_DIAG
@@ -28,9 +28,10 @@ __device__ __forceinline__ unsigned long long diag_now() {
     return t;
 }
 struct DiagTl {
-    unsigned long long t_entry = 0, t_wait = 0, t_mark = 0;
+    unsigned long long t_entry = 0, t_wait = 0, t_mark = 0, t_mark2 = 0;
     __device__ __forceinline__ void entry() { t_entry = diag_now(); }
     __device__ __forceinline__ void mark() { t_mark = diag_now(); }
+    __device__ __forceinline__ void mark2() { t_mark2 = diag_now(); }
     __device__ __forceinline__ void waited() { t_wait = diag_now(); }
     __device__ __forceinline__ void done(uint32_t tag) {
         const unsigned int i = atomicAdd(&g_diag_tl_n, 1u);
@@ -46,6 +47,8 @@ struct DiagTl {
         r.t_wait = t_wait;
         r.t_done = diag_now();
         r.pad = t_mark;
+        r.pad2 = t_mark2;
+        r.pad3 = r.pad4 = r.pad5 = 0;
         g_diag_tl[i] = r;
     }
 };
@@ -67,6 +70,7 @@ struct DiagTl {
     __device__ __forceinline__ void entry() {}
     __device__ __forceinline__ void waited() {}
     __device__ __forceinline__ void mark() {}
+    __device__ __forceinline__ void mark2() {}
     __device__ __forceinline__ void done(uint32_t) {}
 };
 #define AMCU_DIAG_TL(x)

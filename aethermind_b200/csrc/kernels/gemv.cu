@@ -120,13 +120,14 @@ __global__ void __launch_bounds__((NC + 1) * 32, NC == kGemvConsumers ? GEMV_MIN
             int slot = 0;
             uint32_t phase = 0;
             const uint8_t* run = static_cast<const uint8_t*>(p.w) + (size_t)rb0 * G * UB;
+            const uint64_t pol = gemv_weight_policy();
             for (int i = 0; i < total; ++i) {
                 if (i >= S && !mbar_wait(&empty[slot], phase ^ 1u)) {
                     record_device_error(p.err, kErrGemvEmptyWait);
                     break;
                 }
                 mbar_expect_tx(&full[slot], SBY);
-                bulk_g2s(ring + slot * SBY, run + (size_t)i * SBY, SBY, &full[slot]);
+                bulk_g2s_hint(ring + slot * SBY, run + (size_t)i * SBY, SBY, &full[slot], pol);
                 if (++slot == S) {
                     slot = 0;
                     phase ^= 1;
@@ -296,7 +297,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemvThreadsWide, 1)
                 const uint8_t* src = static_cast<const uint8_t*>(p.w) +
                                      ((size_t)(rb0 + r) * G + (size_t)rank * GH + (size_t)j * SU) * UB;
                 mbar_expect_tx(&full[slot], SBY);
-                bulk_g2s(ring + slot * SBY, src, SBY, &full[slot]);
+                bulk_g2s_hint(ring + slot * SBY, src, SBY, &full[slot], gemv_weight_policy());
                 if (++slot == S) {
                     slot = 0;
                     phase ^= 1;

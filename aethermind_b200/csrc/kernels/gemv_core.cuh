@@ -158,6 +158,22 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int64_t rb, i
     }
 }
 
+// L2 policy of the weight stream: each weight byte is read once per decode
+// step, while the KV cache and the activations are read again soon, so the
+// weights go first when L2 evicts.
+#ifndef AMCU_GEMV_EVICT_FIRST
+#define AMCU_GEMV_EVICT_FIRST 1
+#endif
+__device__ __forceinline__ uint64_t gemv_weight_policy() {
+#if AMCU_GEMV_EVICT_FIRST
+    return l2_policy_evict_first();
+#else
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+#endif
+}
+
 constexpr int kXPad = 16;  // bytes of padding per staged activation row
 #ifndef GEMV_MINB
 #define GEMV_MINB 2

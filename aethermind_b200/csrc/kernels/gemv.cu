@@ -137,18 +137,19 @@ __global__ void __launch_bounds__((NC + 1) * 32, NC == kGemvConsumers ? GEMV_MIN
         return;
     }
 
+    __shared__ StageShared stsh;
     pdl_wait();
     pdl_trigger();
     tl.waited();
 
     // ---- stage the activations (fused RMSNorm; INT4: fp16 + group sums)
-    __shared__ StageShared stsh;
     {
         StageCtx sc{static_cast<const __nv_bfloat16*>(p.x), p.x_stride, p.k, M,
                     static_cast<const __nv_bfloat16*>(p.norm_w), p.eps, xs, xrow, sx, &stsh,
                     (int)threadIdx.x, NC * 32, 2};
         stage_activations<W4>(sc);
     }
+    if (threadIdx.x == 0) tl.mark2();  // staged
     const float* row_mul = stsh.row_mul;
     constexpr int NT = NC * 32;
     const float rm0 = 2 * t < M ? row_mul[2 * t] : 1.f, rm1 = 2 * t + 1 < M ? row_mul[2 * t + 1] : 1.f;
@@ -198,6 +199,7 @@ __global__ void __launch_bounds__((NC + 1) * 32, NC == kGemvConsumers ? GEMV_MIN
         for (int j = 0; j < per_row; ++j) stage(r * per_row + j, j * SU, SU);
         finish(rb0 + r);
     }
+    if (threadIdx.x == 0) tl.mark();  // every row block done (thread 0's view)
     if (fail_i >= 0 && warp == 0 && lane == 0) {
         // A wait ran out: stages fail_i .. total - 1 may still be landing.
         // Give them a bounded chance before the CTA's shared memory goes away.

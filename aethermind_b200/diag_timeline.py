@@ -3,8 +3,9 @@
 A library built with ``-DAMCU_DIAG`` (``AMCU_EXTRA_NVCC_FLAGS=-DAMCU_DIAG python
 -m aethermind_b200.build``) logs, for every CTA of the decode GEMV and fused
 attention kernels, its SM and the globaltimer at entry, when its dependency
-wait (griddepcontrol.wait) returned, up to two marks inside the attention
-kernel, and when it was done. This module runs a synthetic 8B W4 generation,
+wait (griddepcontrol.wait) returned, two marks inside the kernel (GEMV:
+activations staged, row blocks done; attention: q staged, key loop done),
+and when it was done. This module runs a synthetic 8B W4 generation,
 takes the log of its last decode steps and prints, per kernel role, medians
 over the layers of:
 
@@ -94,19 +95,22 @@ def main() -> None:
         v = [(g["tw"].min() - prev) / 1e3, (g["tw"].max() - g["tw"].min()) / 1e3,
              (np.median(g["td"]) - g["tw"].min()) / 1e3, (g["td"].max() - g["tw"].min()) / 1e3,
              (g["td"].max() - prev) / 1e3]
-        if g["tag"] >= 2000:
-            v += [(np.median(g["m2"]) - g["tw"].min()) / 1e3, (np.median(g["m1"] - g["m2"])) / 1e3,
-                  (np.median(g["td"] - g["m1"])) / 1e3]
+        # marks: attention = q staged (m2), key loop done (m1); GEMV = activations staged (m2), row blocks done (m1)
+        v += [(np.median(g["m2"]) - g["tw"].min()) / 1e3, (np.median(g["m1"] - g["m2"])) / 1e3,
+              (np.median(g["td"] - g["m1"])) / 1e3]
         stats.setdefault(role(seq, i), []).append(v)
     print(f"decode ms per step (diagnostics build): {dec / 5:.3f}")
     print(f"{'role':10s} {'n':>3s} {'wait-prev':>9s} {'wait-sprd':>9s} {'med-done':>9s} {'max-done':>9s} {'span':>9s}  (us)")
     for k, vs in stats.items():
         a = np.median(np.array([x[:5] for x in vs]), axis=0)
         print(f"{k:10s} {len(vs):3d} " + " ".join(f"{x:9.2f}" for x in a))
-    if "attention" in stats:
-        a = np.median(np.array([x[5:] for x in stats["attention"]]), axis=0)
-        print(f"attention phases (median CTA): q staged + append {a[0]:.2f}, key loop {a[1]:.2f}, "
-              f"merge + barriers + store {a[2]:.2f} us")
+    for k, vs in stats.items():
+        a = np.median(np.array([x[5:] for x in vs]), axis=0)
+        if k == "attention":
+            print(f"attention phases (median CTA): q staged + append {a[0]:.2f}, key loop {a[1]:.2f}, "
+                  f"merge + barriers + store {a[2]:.2f} us")
+        else:
+            print(f"{k} phases (median CTA): staging {a[0]:.2f}, row blocks {a[1]:.2f}, drain {a[2]:.2f} us")
 
 
 if __name__ == "__main__":
